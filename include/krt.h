@@ -1,0 +1,163 @@
+/*
+ * krt.h -- C ABI of the B200 decoder hot path (libkrt.so).
+ *
+ * Plain pointers, sizes and POD structs; no exceptions cross this boundary.
+ * Every entry point returns KRT_OK (0) or a KRT_ERR_* code and records a
+ * message readable with krt_last_error() on the calling thread.  Device
+ * pointers are CUDA device addresses on the current device; `stream` is a
+ * cudaStream_t (NULL = legacy default stream).
+ *
+ * Reference interfaces these entry points replace (paths inside the
+ * Kinetic-RT project):
+ *   krt_fused_rmsnorm_qkv_rope  python/kinetic_rt/fusion_forge.py:21-31 (the
+ *                               Triton kernel's 24-argument signature) and
+ *                               src/AOTEngine.cpp:489-570 (AOTEngine::launch
+ *                               packing the same 24 arguments)
+ *   krt_qkv_rope_decode / _prefill
+ *                               same computation, plus the K/V scatter into
+ *                               BlockManager's pool (include/BlockManager.h:29-95,
+ *                               block ids from src/GraphWrapper.cpp:139-145)
+ *   krt_comm_* / krt_allreduce  include/Communicator.h:15-26 and
+ *                               src/Communicator.cpp:21-27 (all_reduce_async)
+ *   krt_rowparallel_gemm_ar     row-parallel o_proj/down_proj
+ *                               (scripts/export_hf.py:62-65) followed by
+ *                               Communicator::all_reduce_async, as one call
+ */
+#ifndef KRT_H_
+#define KRT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KRT_API __attribute__((visibility("default")))
+#else
+#define KRT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------- status codes */
+#define KRT_OK 0
+#define KRT_ERR_INVALID 1     /* bad argument (null pointer, shape, stride)     */
+#define KRT_ERR_CUDA 2        /* a CUDA runtime call failed                     */
+#define KRT_ERR_UNSUPPORTED 3 /* shape/dtype outside what the kernel handles    */
+#define KRT_ERR_WORKSPACE 4   /* workspace missing or too small                 */
+#define KRT_ERR_DEVICE 5      /* a kernel reported an error in its status word  */
+
+/* dtype codes: the binding's DataType enum (bindings/python_bindings.cpp:19-28) */
+#define KRT_DTYPE_FLOAT32 1
+#define KRT_DTYPE_BFLOAT16 3
+
+/* Message of the last failing call on this thread ("" if none). */
+KRT_API const char* krt_last_error(void);
+
+/* Library version string. */
+KRT_API const char* krt_version(void);
+
+/* -------------------------------------------------------------------------
+ * Reference-compatible fused RMSNorm + QKV projection + RoPE.
+ *
+ * Semantics of fusion_forge.py:21-162 for any d_model (the Triton kernel is
+ * limited to d_model <= 128): per token t,
+ *   x_hat = cast(x_t * rsqrt(mean(x_t^2) + eps) * rms_weight)
+ *   qkv   = qkv_weight @ x_hat (+ qkv_bias)          fp32 accumulation
+ *   q, k, v = qkv split [n_heads*hd | n_kv_heads*hd | n_kv_heads*hd]
+ *   q, k rotated per head: u*cos + rotate_half(u)*sin
+ * cos/sin element for token t, head h, dim d is
+ *   freqs[row * stride_f_seq + (h * freqs_head_stride + d) * stride_f_dim]
+ * with row = positions ? positions[t] : t.  With n_heads = 1 and
+ * head_dim = d_model this is exactly the reference kernel (whose cos/sin use
+ * x's strides, fusion_forge.py:92-93).  CUDA cores, fp32 math; any strides.
+ * ---------------------------------------------------------------------- */
+typedef struct krt_qkv_rope_args {
+  const void* x;          /* [seq_len, d_model]                         */
+  const void* qkv_weight; /* [(n_heads + 2*n_kv_heads)*head_dim, d_model] */
+  const void* qkv_bias;   /* same length as the output rows, or NULL    */
+  const void* rms_weight; /* [d_model]                                  */
+  const void* freqs_cos;
+  const void* freqs_sin;
+  void* q_out; /* [seq_len, n_heads*head_dim]    */
+  void* k_out; /* [seq_len, n_kv_heads*head_dim] */
+  void* v_out; /* [seq_len, n_kv_heads*head_dim] */
+  int32_t seq_len, d_model, n_heads, head_dim;
+  float eps;
+  int64_t stride_x_seq, stride_x_dim;
+  int64_t stride_w_out, stride_w_in;
+  int64_t stride_q_seq, stride_q_dim;
+  int64_t stride_k_seq, stride_k_dim;
+  int64_t stride_v_seq, stride_v_dim;
+  /* extensions (zero-initialised structs give the reference behaviour) */
+  int32_t dtype;             /* KRT_DTYPE_*, 0 = float32                 */
+  int32_t n_kv_heads;        /* 0 = n_heads                              */
+  int32_t freqs_dtype;       /* 0 = same as dtype                        */
+  int32_t freqs_head_stride; /* -1 = head_dim (per-head columns), 0 = shared row */
+  int64_t stride_f_seq, stride_f_dim; /* 0,0 = x's strides (reference)   */
+  const int32_t* positions;  /* NULL = token index                       */
+} krt_qkv_rope_args;
+
+KRT_API int krt_fused_rmsnorm_qkv_rope(const krt_qkv_rope_args* args, void* stream);
+
+/* -------------------------------------------------------------------------
+ * Paged fused RMSNorm + QKV + RoPE + K/V scatter (bf16, tcgen05 tensor cores).
+ *
+ * Same math as above with GQA, bf16 activations/weights, fp32 RoPE tables
+ * indexed by position, and K/V written straight into the paged KV pool:
+ *   slot(t)  = block_table[token_seq[t] * block_table_stride
+ *                          + positions[t] / tokens_per_block]
+ *   pool byte offset = (slot * tokens_per_block + positions[t] % tokens_per_block)
+ *                      * token_bytes,  token_bytes = 2 * n_kv_heads * head_dim * 2
+ *   token layout     = [K | V][kv_head][head_dim] bf16
+ * i.e. BlockManager's pool (block i at pool + i * tokens_per_block * token_bytes).
+ * Block ids outside [0, num_blocks), positions outside [0, max_position) or
+ * block-table columns outside the table skip the write and set KRT_ERR_DEVICE
+ * in the status word (krt_read_status).
+ *
+ * decode : num_tokens <= 256, split-K across the GPU; needs a workspace of
+ *          krt_qkv_rope_decode_workspace_size() bytes, zero-filled once when
+ *          allocated (the kernel leaves it zeroed after every call).
+ * prefill: any num_tokens; needs krt_qkv_rope_prefill_workspace_size() bytes.
+ * head_dim must be 128; d_model a multiple of 64.
+ * ---------------------------------------------------------------------- */
+typedef struct krt_qkv_paged_args {
+  const void* x;          /* bf16 [num_tokens, d_model], row stride x_stride */
+  const void* qkv_weight; /* bf16 [(n_heads+2*n_kv_heads)*128, d_model], dense rows */
+  const void* qkv_bias;   /* bf16 [(n_heads+2*n_kv_heads)*128] or NULL */
+  const void* rms_weight; /* bf16 [d_model] */
+  const float* rope_cos;  /* fp32 [max_position, 128] */
+  const float* rope_sin;  /* fp32 [max_position, 128] */
+  const int32_t* positions;   /* [num_tokens] */
+  const int32_t* token_seq;   /* [num_tokens] row of block_table for each token */
+  const int32_t* block_table; /* [num_seqs, block_table_stride] */
+  void* kv_pool;              /* bf16, num_blocks * tokens_per_block * token_bytes bytes */
+  void* q_out;                /* bf16 [num_tokens, n_heads, 128] (row stride q_stride) */
+  void* k_out;                /* optional dense bf16 [num_tokens, n_kv_heads, 128] */
+  void* v_out;                /* optional dense bf16 [num_tokens, n_kv_heads, 128] */
+  int32_t num_tokens, d_model, n_heads, n_kv_heads, head_dim;
+  int32_t x_stride, q_stride;
+  int32_t max_position;
+  int32_t num_seqs, block_table_stride, num_blocks, tokens_per_block;
+  float eps;
+  void* workspace;
+  size_t workspace_bytes;
+} krt_qkv_paged_args;
+
+KRT_API size_t krt_qkv_rope_decode_workspace_size(int32_t num_tokens, int32_t d_model, int32_t n_heads,
+                                          int32_t n_kv_heads, int32_t head_dim);
+KRT_API int krt_qkv_rope_decode(const krt_qkv_paged_args* args, void* stream);
+
+KRT_API size_t krt_qkv_rope_prefill_workspace_size(int32_t num_tokens, int32_t d_model, int32_t n_heads,
+                                           int32_t n_kv_heads, int32_t head_dim);
+KRT_API int krt_qkv_rope_prefill(const krt_qkv_paged_args* args, void* stream);
+
+/* Copy the device status word of a workspace to the host (synchronises the
+ * stream), clear it, and return KRT_OK or KRT_ERR_DEVICE with the bits in
+ * *bits. */
+KRT_API int krt_read_status(void* workspace, void* stream, int32_t* bits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KRT_H_ */

@@ -1,0 +1,416 @@
+// C-ABI entry points of libkrt.so (declared in include/krt.h).
+//
+// Argument validation, launch-shape selection, TMA descriptor encoding and
+// error reporting live here; the kernels are in qkv_generic.cu,
+// qkv_decode.cu and qkv_prefill.cu.  Nothing here allocates device memory:
+// callers pass every buffer, including workspaces.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <string>
+
+#include "../../include/krt.h"
+#include "capi_internal.h"
+#include "qkv_generic.cuh"
+#include "qkv_paged.cuh"
+
+namespace krt {
+
+namespace {
+thread_local std::string g_last_error;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(KRT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int clear_error() {
+  g_last_error.clear();
+  return KRT_OK;
+}
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a row pitch
+// of `pitch_elems`, box = [box_rows, 64 cols], 128-byte swizzle.
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                      uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(KRT_ERR_INVALID, "TMA base address must be 16-byte aligned");
+  if ((pitch_elems * 2) % 16 != 0) return set_error(KRT_ERR_INVALID, "row pitch must be a multiple of 16 bytes");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return KRT_OK;
+}
+
+// 3-D view of a row-major bf16 [rows, cols] matrix as [cols/64][rows][64]:
+// one box = `kc` consecutive 64-column chunks of `box_rows` rows, landing in
+// shared memory as kc back-to-back [box_rows x 64] 128-byte-swizzled tiles,
+// so each row contributes kc * 128 contiguous bytes per request.
+int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                      uint32_t box_rows, uint32_t kc) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(KRT_ERR_INVALID, "TMA base address must be 16-byte aligned");
+  if ((pitch_elems * 2) % 16 != 0) return set_error(KRT_ERR_INVALID, "row pitch must be a multiple of 16 bytes");
+  if (cols % 64 != 0) return set_error(KRT_ERR_INVALID, "columns must be a multiple of 64");
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {pitch_elems * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, kc};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (CUresult %d)", (int)r);
+  return KRT_OK;
+}
+
+}  // namespace krt
+
+using namespace krt;
+
+extern "C" const char* krt_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" const char* krt_version(void) { return "kinetic-rt-b200 0.1 (sm_100a)"; }
+
+// ------------------------------------------------------------------ generic
+extern "C" int krt_fused_rmsnorm_qkv_rope(const krt_qkv_rope_args* a, void* stream) {
+  if (!a) return set_error(KRT_ERR_INVALID, "krt_fused_rmsnorm_qkv_rope: args is NULL");
+  if (!a->x || !a->qkv_weight || !a->rms_weight || !a->freqs_cos || !a->freqs_sin || !a->q_out || !a->k_out ||
+      !a->v_out)
+    return set_error(KRT_ERR_INVALID,
+                     "Cannot launch fused_rmsnorm_qkv_rope: descriptor is missing required weight, frequency, or "
+                     "Q/K/V buffers.");
+  if (a->seq_len <= 0 || a->d_model <= 0 || a->n_heads <= 0 || a->head_dim <= 0)
+    return set_error(KRT_ERR_INVALID,
+                     "Cannot launch fused_rmsnorm_qkv_rope: seq_len, d_model, n_heads, and head_dim must be positive.");
+  if (a->head_dim % 2 != 0) return set_error(KRT_ERR_INVALID, "head_dim must be even for rotate-half RoPE");
+  const int dtype = a->dtype == 0 ? KRT_DTYPE_FLOAT32 : a->dtype;
+  const int fdtype = a->freqs_dtype == 0 ? dtype : a->freqs_dtype;
+  if ((dtype != KRT_DTYPE_FLOAT32 && dtype != KRT_DTYPE_BFLOAT16) ||
+      (fdtype != KRT_DTYPE_FLOAT32 && fdtype != KRT_DTYPE_BFLOAT16))
+    return set_error(KRT_ERR_UNSUPPORTED, "fused_rmsnorm_qkv_rope supports float32 and bfloat16 only");
+  GenericArgs g;
+  g.x = a->x;
+  g.w = a->qkv_weight;
+  g.bias = a->qkv_bias;
+  g.gamma = a->rms_weight;
+  g.cos = a->freqs_cos;
+  g.sin = a->freqs_sin;
+  g.q = a->q_out;
+  g.k = a->k_out;
+  g.v = a->v_out;
+  g.seq_len = a->seq_len;
+  g.d_model = a->d_model;
+  g.n_heads = a->n_heads;
+  g.n_kv_heads = a->n_kv_heads > 0 ? a->n_kv_heads : a->n_heads;
+  g.head_dim = a->head_dim;
+  g.eps = a->eps;
+  g.sx_seq = a->stride_x_seq;
+  g.sx_dim = a->stride_x_dim;
+  g.sw_out = a->stride_w_out;
+  g.sw_in = a->stride_w_in;
+  g.sq_seq = a->stride_q_seq;
+  g.sq_dim = a->stride_q_dim;
+  g.sk_seq = a->stride_k_seq;
+  g.sk_dim = a->stride_k_dim;
+  g.sv_seq = a->stride_v_seq;
+  g.sv_dim = a->stride_v_dim;
+  const bool f_default = a->stride_f_seq == 0 && a->stride_f_dim == 0;
+  g.sf_seq = f_default ? a->stride_x_seq : a->stride_f_seq;
+  g.sf_dim = f_default ? a->stride_x_dim : a->stride_f_dim;
+  g.f_head_stride = a->freqs_head_stride < 0 ? a->head_dim : a->freqs_head_stride;
+  g.positions = a->positions;
+  cudaError_t e = launch_qkv_rope_generic(g, dtype, fdtype, 0, 0, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_error(e, "fused_rmsnorm_qkv_rope launch");
+  return clear_error();
+}
+
+// ------------------------------------------------------------------- paged
+namespace {
+
+int paged_common_checks(const krt_qkv_paged_args* a, const char* name) {
+  if (!a) return set_error(KRT_ERR_INVALID, "%s: args is NULL", name);
+  if (!a->x || !a->qkv_weight || !a->rms_weight || !a->rope_cos || !a->rope_sin || !a->positions ||
+      !a->token_seq || !a->block_table || !a->kv_pool || !a->q_out)
+    return set_error(KRT_ERR_INVALID, "%s: a required pointer is NULL", name);
+  if (a->num_tokens <= 0 || a->d_model <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0)
+    return set_error(KRT_ERR_INVALID, "%s: num_tokens, d_model, n_heads and n_kv_heads must be positive", name);
+  if (a->head_dim != kHeadDim) return set_error(KRT_ERR_UNSUPPORTED, "%s: head_dim must be 128", name);
+  if (a->d_model % kBK != 0) return set_error(KRT_ERR_UNSUPPORTED, "%s: d_model must be a multiple of 64", name);
+  if (a->n_heads + 2 * a->n_kv_heads > kMaxTiles)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: too many heads", name);
+  if (a->x_stride < a->d_model || a->x_stride % 8 != 0)
+    return set_error(KRT_ERR_INVALID, "%s: x_stride must be >= d_model and a multiple of 8", name);
+  if (a->q_stride < a->n_heads * kHeadDim)
+    return set_error(KRT_ERR_INVALID, "%s: q_stride must be >= n_heads * 128", name);
+  if ((reinterpret_cast<uintptr_t>(a->x) & 15) || (reinterpret_cast<uintptr_t>(a->rms_weight) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->qkv_weight) & 15) || (reinterpret_cast<uintptr_t>(a->q_out) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->kv_pool) & 15) || (reinterpret_cast<uintptr_t>(a->k_out) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->v_out) & 15) || (reinterpret_cast<uintptr_t>(a->rope_cos) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->rope_sin) & 15))
+    return set_error(KRT_ERR_INVALID, "%s: tensors must be 16-byte aligned", name);
+  if (a->q_stride % 8 != 0) return set_error(KRT_ERR_INVALID, "%s: q_stride must be a multiple of 8", name);
+  if (a->max_position <= 0 || a->num_seqs <= 0 || a->block_table_stride <= 0 || a->num_blocks <= 0 ||
+      a->tokens_per_block <= 0)
+    return set_error(KRT_ERR_INVALID, "%s: paged-cache geometry must be positive", name);
+  if (!a->workspace) return set_error(KRT_ERR_WORKSPACE, "%s: workspace is NULL", name);
+  return KRT_OK;
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+int decode_stages(int n_pad, int kc) {
+  for (int st = kMaxStages; st >= 1; --st)
+    if (decode_smem_bytes(st, n_pad, kc) <= 227 * 1024) return st;
+  return 0;
+}
+
+// 64-column chunks per decode pipeline stage (TMA box depth): the deepest of
+// 4, 2, 1 that divides the k-blocks and still leaves two pipeline stages.
+// KRT_DECODE_KC overrides the starting value for tuning.
+int decode_kc(int num_kb, int n_pad) {
+  int kc = env_int("KRT_DECODE_KC", 4);
+  if (kc < 1) kc = 1;
+  while (kc > 1 && ((num_kb % kc) != 0 || decode_stages(n_pad, kc) < 2)) kc >>= 1;
+  return kc;
+}
+
+// Split-K factor = cluster size along gridDim.y: as many splits as fit
+// (tiles * splits <= #SMs, at most 8 = portable cluster size) while every
+// cluster of the grid can be resident at once.  KRT_DECODE_SPLITS overrides.
+int decode_splits(int tiles, int num_kc, int n_pad, int stages, int kc) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, tiles, num_kc, n_pad, stages, kc);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int s = env_int("KRT_DECODE_SPLITS", 0);
+  if (s <= 0) {
+    s = device_sm_count() / tiles;
+    if (s > 8) s = 8;
+    if (s > num_kc) s = num_kc;
+    if (s < 1) s = 1;
+    while (s > 1 && decode_max_active_clusters(s, n_pad, stages, kc) < tiles) --s;
+  } else if (s > num_kc) {
+    s = num_kc;
+  }
+  cache[key] = s;
+  return s;
+}
+
+}  // namespace
+
+extern "C" size_t krt_qkv_rope_decode_workspace_size(int32_t num_tokens, int32_t d_model, int32_t n_heads,
+                                                     int32_t n_kv_heads, int32_t head_dim) {
+  if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0 || head_dim != kHeadDim || n_heads <= 0 ||
+      n_kv_heads <= 0)
+    return 0;
+  return ws_layout(num_tokens, d_model, 0).total;
+}
+
+extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
+  int rc = paged_common_checks(a, "krt_qkv_rope_decode");
+  if (rc) return rc;
+  if (a->num_tokens > 256)
+    return set_error(KRT_ERR_UNSUPPORTED, "krt_qkv_rope_decode: num_tokens must be <= 256 (use the prefill path)");
+  const int tiles = a->n_heads + 2 * a->n_kv_heads;
+  const int num_kb = a->d_model / kBK;
+  const size_t need =
+      krt_qkv_rope_decode_workspace_size(a->num_tokens, a->d_model, a->n_heads, a->n_kv_heads, a->head_dim);
+  if (a->workspace_bytes < need)
+    return set_error(KRT_ERR_WORKSPACE, "krt_qkv_rope_decode: workspace of %zu bytes, %zu needed",
+                     a->workspace_bytes, need);
+  PagedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = static_cast<const __nv_bfloat16*>(a->x);
+  p.bias = static_cast<const __nv_bfloat16*>(a->qkv_bias);
+  p.gamma = static_cast<const __nv_bfloat16*>(a->rms_weight);
+  p.cos = a->rope_cos;
+  p.sin = a->rope_sin;
+  p.positions = a->positions;
+  p.token_seq = a->token_seq;
+  p.block_table = a->block_table;
+  p.pool = static_cast<__nv_bfloat16*>(a->kv_pool);
+  p.q = static_cast<__nv_bfloat16*>(a->q_out);
+  p.k = static_cast<__nv_bfloat16*>(a->k_out);
+  p.v = static_cast<__nv_bfloat16*>(a->v_out);
+  p.num_tokens = a->num_tokens;
+  p.n_pad = (a->num_tokens + 15) / 16 * 16;
+  p.d_model = a->d_model;
+  p.n_heads = a->n_heads;
+  p.n_kv_heads = a->n_kv_heads;
+  p.x_stride = a->x_stride;
+  p.q_stride = a->q_stride;
+  p.max_position = a->max_position;
+  p.num_seqs = a->num_seqs;
+  p.bt_stride = a->block_table_stride;
+  p.num_blocks = a->num_blocks;
+  p.tokens_per_block = a->tokens_per_block;
+  p.eps = a->eps;
+  p.kc = decode_kc(num_kb, p.n_pad);
+  p.stages = decode_stages(p.n_pad, p.kc);
+  p.splits = decode_splits(tiles, num_kb / p.kc, p.n_pad, p.stages, p.kc);
+  int cols = 32;
+  while (cols < p.n_pad) cols <<= 1;
+  p.tmem_cols = cols;
+  char* ws = static_cast<char*>(a->workspace);
+  const WsLayout L = ws_layout(p.num_tokens, p.d_model, 0);
+  p.status = reinterpret_cast<int*>(ws);
+  p.tok_pos = reinterpret_cast<int*>(ws + L.pos_off);
+  p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
+  p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
+
+  CUtensorMap tmap_w, tmap_x;
+  rc = make_tmap_bf16_3d(&tmap_w, a->qkv_weight, (uint64_t)tiles * kHeadDim, (uint64_t)a->d_model,
+                         (uint64_t)a->d_model, 128, (uint32_t)p.kc);
+  if (rc) return rc;
+  rc = make_tmap_bf16_3d(&tmap_x, p.xhat, (uint64_t)p.num_tokens, (uint64_t)a->d_model, (uint64_t)a->d_model,
+                         (uint32_t)p.n_pad, (uint32_t)p.kc);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = launch_qkv_prep(p, s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_decode prep launch");
+  e = launch_qkv_rope_decode(tmap_w, tmap_x, p, tiles, s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_decode launch");
+  return clear_error();
+}
+
+extern "C" int krt_read_status(void* workspace, void* stream, int32_t* bits) {
+  if (!workspace || !bits) return set_error(KRT_ERR_INVALID, "krt_read_status: NULL argument");
+  int v = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_read_status");
+  *bits = v;
+  if (v != 0) {
+    // An aborted launch can leave split-K counters behind: clear the header.
+    e = cudaMemsetAsync(workspace, 0, kWsHeaderBytes, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_error(e, "krt_read_status clear");
+    return set_error(KRT_ERR_DEVICE, "kernel status bits 0x%x", v);
+  }
+  return clear_error();
+}
+
+// ------------------------------------------------------------------ prefill
+extern "C" size_t krt_qkv_rope_prefill_workspace_size(int32_t num_tokens, int32_t d_model, int32_t n_heads,
+                                                      int32_t n_kv_heads, int32_t head_dim) {
+  (void)n_heads;
+  (void)n_kv_heads;
+  if (num_tokens <= 0 || d_model <= 0 || head_dim != kHeadDim) return 0;
+  return ws_layout(num_tokens, d_model, 0).total;
+}
+
+extern "C" int krt_qkv_rope_prefill(const krt_qkv_paged_args* a, void* stream) {
+  int rc = paged_common_checks(a, "krt_qkv_rope_prefill");
+  if (rc) return rc;
+  const int tiles = a->n_heads + 2 * a->n_kv_heads;
+  const size_t need =
+      krt_qkv_rope_prefill_workspace_size(a->num_tokens, a->d_model, a->n_heads, a->n_kv_heads, a->head_dim);
+  if (a->workspace_bytes < need)
+    return set_error(KRT_ERR_WORKSPACE, "krt_qkv_rope_prefill: workspace of %zu bytes, %zu needed",
+                     a->workspace_bytes, need);
+  PagedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = static_cast<const __nv_bfloat16*>(a->x);
+  p.bias = static_cast<const __nv_bfloat16*>(a->qkv_bias);
+  p.gamma = static_cast<const __nv_bfloat16*>(a->rms_weight);
+  p.cos = a->rope_cos;
+  p.sin = a->rope_sin;
+  p.positions = a->positions;
+  p.token_seq = a->token_seq;
+  p.block_table = a->block_table;
+  p.pool = static_cast<__nv_bfloat16*>(a->kv_pool);
+  p.q = static_cast<__nv_bfloat16*>(a->q_out);
+  p.k = static_cast<__nv_bfloat16*>(a->k_out);
+  p.v = static_cast<__nv_bfloat16*>(a->v_out);
+  p.num_tokens = a->num_tokens;
+  p.n_pad = a->num_tokens;
+  p.d_model = a->d_model;
+  p.n_heads = a->n_heads;
+  p.n_kv_heads = a->n_kv_heads;
+  p.x_stride = a->x_stride;
+  p.q_stride = a->q_stride;
+  p.max_position = a->max_position;
+  p.num_seqs = a->num_seqs;
+  p.bt_stride = a->block_table_stride;
+  p.num_blocks = a->num_blocks;
+  p.tokens_per_block = a->tokens_per_block;
+  p.eps = a->eps;
+  char* ws = static_cast<char*>(a->workspace);
+  const WsLayout L = ws_layout(p.num_tokens, p.d_model, 0);
+  p.status = reinterpret_cast<int*>(ws);
+  p.tok_pos = reinterpret_cast<int*>(ws + L.pos_off);
+  p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
+  p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
+
+  CUtensorMap tmap_w, tmap_x;
+  rc = make_tmap_bf16_2d(&tmap_w, a->qkv_weight, (uint64_t)tiles * kHeadDim, (uint64_t)a->d_model,
+                         (uint64_t)a->d_model, 128);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tmap_x, p.xhat, (uint64_t)a->num_tokens, (uint64_t)a->d_model, (uint64_t)a->d_model, 256);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = launch_qkv_prep(p, s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_prefill prep launch");
+  e = launch_qkv_rope_prefill(tmap_w, tmap_x, p, tiles, s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_prefill launch");
+  return clear_error();
+}

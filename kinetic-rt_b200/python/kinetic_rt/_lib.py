@@ -1,0 +1,184 @@
+"""ctypes binding of libkrt.so, the C ABI declared in include/krt.h.
+
+This is the thinnest possible layer: struct mirrors, argument marshalling
+from torch tensors (data_ptr / strides / current stream) and error
+translation.  Loading fails loudly when the library is missing; there is no
+fallback implementation.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libkrt.so")
+
+KRT_OK = 0
+KRT_ERR_INVALID = 1
+KRT_ERR_CUDA = 2
+KRT_ERR_UNSUPPORTED = 3
+KRT_ERR_WORKSPACE = 4
+KRT_ERR_DEVICE = 5
+KRT_DTYPE_FLOAT32 = 1
+KRT_DTYPE_BFLOAT16 = 3
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+
+
+class QkvRopeArgs(ctypes.Structure):
+    """krt_qkv_rope_args"""
+    _fields_ = [
+        ("x", _vp), ("qkv_weight", _vp), ("qkv_bias", _vp), ("rms_weight", _vp),
+        ("freqs_cos", _vp), ("freqs_sin", _vp), ("q_out", _vp), ("k_out", _vp), ("v_out", _vp),
+        ("seq_len", _i32), ("d_model", _i32), ("n_heads", _i32), ("head_dim", _i32),
+        ("eps", ctypes.c_float),
+        ("stride_x_seq", _i64), ("stride_x_dim", _i64), ("stride_w_out", _i64), ("stride_w_in", _i64),
+        ("stride_q_seq", _i64), ("stride_q_dim", _i64), ("stride_k_seq", _i64), ("stride_k_dim", _i64),
+        ("stride_v_seq", _i64), ("stride_v_dim", _i64),
+        ("dtype", _i32), ("n_kv_heads", _i32), ("freqs_dtype", _i32), ("freqs_head_stride", _i32),
+        ("stride_f_seq", _i64), ("stride_f_dim", _i64), ("positions", _vp),
+    ]
+
+
+class QkvPagedArgs(ctypes.Structure):
+    """krt_qkv_paged_args"""
+    _fields_ = [
+        ("x", _vp), ("qkv_weight", _vp), ("qkv_bias", _vp), ("rms_weight", _vp),
+        ("rope_cos", _vp), ("rope_sin", _vp), ("positions", _vp), ("token_seq", _vp),
+        ("block_table", _vp), ("kv_pool", _vp), ("q_out", _vp), ("k_out", _vp), ("v_out", _vp),
+        ("num_tokens", _i32), ("d_model", _i32), ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32),
+        ("x_stride", _i32), ("q_stride", _i32), ("max_position", _i32),
+        ("num_seqs", _i32), ("block_table_stride", _i32), ("num_blocks", _i32), ("tokens_per_block", _i32),
+        ("eps", ctypes.c_float), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# Every symbol include/krt.h declares, with (restype, argtypes).
+SIGNATURES = {
+    "krt_last_error": (ctypes.c_char_p, []),
+    "krt_version": (ctypes.c_char_p, []),
+    "krt_fused_rmsnorm_qkv_rope": (ctypes.c_int, [ctypes.POINTER(QkvRopeArgs), _vp]),
+    "krt_qkv_rope_decode_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
+    "krt_qkv_rope_decode": (ctypes.c_int, [ctypes.POINTER(QkvPagedArgs), _vp]),
+    "krt_qkv_rope_prefill_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
+    "krt_qkv_rope_prefill": (ctypes.c_int, [ctypes.POINTER(QkvPagedArgs), _vp]),
+    "krt_read_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i32)]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load libkrt.so once.  Raises ImportError when it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"libkrt.so not found at {LIB_PATH}; run kinetic-rt_b200/build.py")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(h, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = h
+    return _lib
+
+
+class KrtError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(msg)
+        self.code = code
+
+
+def check(rc):
+    if rc != KRT_OK:
+        msg = lib().krt_last_error().decode()
+        if rc in (KRT_ERR_INVALID, KRT_ERR_UNSUPPORTED, KRT_ERR_WORKSPACE):
+            err = ValueError(msg)
+            err.code = rc
+            raise err
+        raise KrtError(rc, msg)
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is not None:
+        return ctypes.c_void_p(int(stream))
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dtype_code(t):
+    import torch
+    if t.dtype == torch.float32:
+        return KRT_DTYPE_FLOAT32
+    if t.dtype == torch.bfloat16:
+        return KRT_DTYPE_BFLOAT16
+    raise ValueError(f"unsupported dtype {t.dtype}; float32 and bfloat16 are supported")
+
+
+def fused_rmsnorm_qkv_rope(x, qkv_weight, qkv_bias, rms_weight, freqs_cos, freqs_sin, q_out, k_out, v_out,
+                           seq_len, d_model, n_heads, head_dim, eps, strides, n_kv_heads=0,
+                           freqs_strides=None, freqs_head_stride=-1, positions=None, stream=None):
+    """Generic CUDA-core path (krt_fused_rmsnorm_qkv_rope) on device tensors.
+    `strides` = the reference's ten strides in argument order
+    (fusion_forge.py:26-30)."""
+    a = QkvRopeArgs()
+    a.x, a.qkv_weight, a.qkv_bias, a.rms_weight = _ptr(x), _ptr(qkv_weight), _ptr(qkv_bias), _ptr(rms_weight)
+    a.freqs_cos, a.freqs_sin = _ptr(freqs_cos), _ptr(freqs_sin)
+    a.q_out, a.k_out, a.v_out = _ptr(q_out), _ptr(k_out), _ptr(v_out)
+    a.seq_len, a.d_model, a.n_heads, a.head_dim, a.eps = int(seq_len), int(d_model), int(n_heads), int(head_dim), float(eps)
+    (a.stride_x_seq, a.stride_x_dim, a.stride_w_out, a.stride_w_in, a.stride_q_seq, a.stride_q_dim,
+     a.stride_k_seq, a.stride_k_dim, a.stride_v_seq, a.stride_v_dim) = [int(s) for s in strides]
+    a.dtype = _dtype_code(x)
+    a.freqs_dtype = _dtype_code(freqs_cos)
+    a.n_kv_heads = int(n_kv_heads)
+    a.freqs_head_stride = int(freqs_head_stride)
+    if freqs_strides is not None:
+        a.stride_f_seq, a.stride_f_dim = [int(s) for s in freqs_strides]
+    a.positions = _ptr(positions)
+    check(lib().krt_fused_rmsnorm_qkv_rope(ctypes.byref(a), _stream(stream)))
+
+
+def decode_workspace_bytes(num_tokens, d_model, n_heads, n_kv_heads, head_dim=128):
+    return int(lib().krt_qkv_rope_decode_workspace_size(num_tokens, d_model, n_heads, n_kv_heads, head_dim))
+
+
+def prefill_workspace_bytes(num_tokens, d_model, n_heads, n_kv_heads, head_dim=128):
+    return int(lib().krt_qkv_rope_prefill_workspace_size(num_tokens, d_model, n_heads, n_kv_heads, head_dim))
+
+
+def paged_args(x, qkv_weight, qkv_bias, rms_weight, rope_cos, rope_sin, positions, token_seq, block_table,
+               kv_pool, q_out, n_heads, n_kv_heads, num_blocks, tokens_per_block, workspace, eps=1e-5,
+               k_out=None, v_out=None, head_dim=128):
+    a = QkvPagedArgs()
+    a.x, a.qkv_weight, a.qkv_bias, a.rms_weight = _ptr(x), _ptr(qkv_weight), _ptr(qkv_bias), _ptr(rms_weight)
+    a.rope_cos, a.rope_sin = _ptr(rope_cos), _ptr(rope_sin)
+    a.positions, a.token_seq, a.block_table = _ptr(positions), _ptr(token_seq), _ptr(block_table)
+    a.kv_pool, a.q_out, a.k_out, a.v_out = _ptr(kv_pool), _ptr(q_out), _ptr(k_out), _ptr(v_out)
+    a.num_tokens, a.d_model = int(x.shape[0]), int(x.shape[1])
+    a.n_heads, a.n_kv_heads, a.head_dim = int(n_heads), int(n_kv_heads), int(head_dim)
+    a.x_stride, a.q_stride = int(x.stride(0)), int(q_out.stride(0))
+    a.max_position = int(rope_cos.shape[0])
+    a.num_seqs, a.block_table_stride = int(block_table.shape[0]), int(block_table.stride(0))
+    a.num_blocks, a.tokens_per_block = int(num_blocks), int(tokens_per_block)
+    a.eps = float(eps)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    return a
+
+
+def qkv_rope_decode(args, stream=None):
+    check(lib().krt_qkv_rope_decode(ctypes.byref(args), _stream(stream)))
+
+
+def qkv_rope_prefill(args, stream=None):
+    check(lib().krt_qkv_rope_prefill(ctypes.byref(args), _stream(stream)))
+
+
+def read_status(workspace, stream=None):
+    bits = _i32(0)
+    rc = lib().krt_read_status(_ptr(workspace), _stream(stream), ctypes.byref(bits))
+    return rc, bits.value
