@@ -157,6 +157,61 @@ KRT_API int krt_qkv_rope_prefill(const krt_qkv_paged_args* args, void* stream);
  * *bits. */
 KRT_API int krt_read_status(void* workspace, void* stream, int32_t* bits);
 
+/* -------------------------------------------------------------------------
+ * Communicator: symmetric peer buffers over NVLink / NVSwitch.
+ *
+ * Replaces Communicator(rank, world_size) (include/Communicator.h:15-26),
+ * whose RCCL backend the reference left commented out
+ * (src/Communicator.cpp:10-27).  One process per GPU:
+ *   krt_comm_create      allocates this rank's buffer on the current device
+ *                        (sized for outputs of up to max_n_out features)
+ *   krt_comm_ipc_handle  writes its CUDA IPC handle (krt_comm_handle_size bytes)
+ *   krt_comm_open_peers  maps every rank's buffer; `handles` holds world_size
+ *                        handles in rank order (this rank's is skipped)
+ * A world_size of 1 needs no peers.  Collectives of one communicator must be
+ * issued on one stream per rank, in the same order on every rank.
+ * ---------------------------------------------------------------------- */
+typedef struct krt_comm krt_comm;
+
+KRT_API int krt_comm_create(int32_t rank, int32_t world_size, int32_t max_n_out, krt_comm** out);
+KRT_API size_t krt_comm_handle_size(void);
+KRT_API int krt_comm_ipc_handle(krt_comm* comm, void* handle_out);
+KRT_API int krt_comm_open_peers(krt_comm* comm, const void* handles);
+KRT_API int krt_comm_destroy(krt_comm* comm);
+
+/* Allreduce-sum of `count` elements (Communicator::all_reduce_async,
+ * src/Communicator.cpp:21-27; every rank's recv receives the elementwise sum
+ * of all ranks' send, tests/mock_rccl.h:51-62).  dtype: KRT_DTYPE_FLOAT32
+ * (0 is accepted as float32, the mock backend's code, tests/mock_rccl.h:14)
+ * or KRT_DTYPE_BFLOAT16; the sum is taken in fp32 in rank order, so every
+ * rank gets bit-identical results.  `status` is a device int (a workspace
+ * header, krt_read_status) that records peer-wait timeouts. */
+KRT_API int krt_allreduce(krt_comm* comm, const void* send, void* recv, size_t count, int32_t dtype, void* status,
+                          void* stream);
+
+/* -------------------------------------------------------------------------
+ * Row-parallel GEMM fused with the allreduce (o_proj / down_proj under TP).
+ *
+ * Rank r holds W[:, K_r] and X[:, K_r] (the torch.chunk(dim=1) shards of
+ * scripts/export_hf.py:62-65); every rank receives
+ *   Y = sum_r X[:, K_r] W[:, K_r]^T          (bf16 out, fp32 accumulation)
+ * in one call: tcgen05 GEMM whose epilogue reduce-scatters fp32 partials into
+ * the owners' peer buffers and all-gathers the bf16 result, with no separate
+ * collective.  comm may be NULL for a single GPU.  Any num_tokens (launched
+ * in slices of 256); k_local % 64 == 0, n_out % 128 == 0.
+ * ---------------------------------------------------------------------- */
+typedef struct krt_gemm_ar_args {
+  const void* x;      /* bf16 [num_tokens, k_local], row stride x_stride */
+  const void* weight; /* bf16 [n_out, k_local], dense rows */
+  void* y;            /* bf16 [num_tokens, n_out], row stride y_stride */
+  int32_t num_tokens, k_local, n_out, x_stride, y_stride;
+  void* workspace;    /* krt_rowparallel_gemm_ar_workspace_size() bytes, zeroed once */
+  size_t workspace_bytes;
+} krt_gemm_ar_args;
+
+KRT_API size_t krt_rowparallel_gemm_ar_workspace_size(void);
+KRT_API int krt_rowparallel_gemm_ar(krt_comm* comm, const krt_gemm_ar_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,4 +41,11 @@ size_t prefill_smem_bytes();
 cudaError_t launch_qkv_rope_prefill(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                     int tiles_per_block, cudaStream_t stream);
 
+// gemm_ar.cu
+struct GemmArParams;
+size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc);
+int gemm_ar_max_active_clusters(int splits, int n_pad, int stages, int kc);
+cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmArParams& p,
+                                       int tiles, cudaStream_t stream);
+
 }  // namespace krt

@@ -1,0 +1,365 @@
+// Communicator plumbing of the C ABI (krt_comm_*), the standalone allreduce
+// and the entry point of the fused row-parallel GEMM + allreduce.
+//
+// Setup (not on the hot path): krt_comm_create allocates this rank's
+// symmetric buffer (layout in comm.h), zero-fills it and exports a CUDA IPC
+// handle; the caller exchanges the handles (e.g. torch.distributed
+// all_gather_object) and passes all of them to krt_comm_open_peers, which
+// maps every peer's buffer.  Ranks are processes, one GPU each.
+//
+// krt_allreduce is the reference's Communicator::all_reduce_async
+// (src/Communicator.cpp:21-27; semantics tests/mock_rccl.h:51-62: every
+// rank receives the elementwise sum of all ranks' send buffers), done as a
+// two-shot exchange over the mapped peer buffers: rank o owns the o-th slice,
+// every rank pushes its slice o to o, o sums in rank order and pushes the
+// result to everyone.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <new>
+
+#include "../../include/krt.h"
+#include "capi_internal.h"
+#include "comm.h"
+#include "ptx.cuh"
+#include "qkv_paged.cuh"
+
+struct krt_comm {
+  int rank = 0, world = 1, device = 0, max_n = 0;
+  krt::CommLayout L;
+  char* local = nullptr;
+  char* peer[krt::kMaxWorld] = {};
+  bool peers_open = false;
+};
+
+namespace krt {
+
+// ------------------------------------------------------ standalone allreduce
+constexpr int kArThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v) {
+  return static_cast<float>(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <typename T>
+__device__ __forceinline__ T from_f32(float v) {
+  return static_cast<T>(v);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// One launch reduces `count` elements: staging row q (count floats) holds
+// rank q's copy of the owner's slice, the result area holds count elements.  CTA b handles
+// the b-th sub-range of every rank's slice.
+template <typename T>
+__global__ void __launch_bounds__(kArThreads) allreduce_kernel(const T* __restrict__ send, T* __restrict__ recv,
+                                                               long long count, CommView cv, int* status) {
+  __shared__ int ok_s;
+  const int world = cv.world, me = cv.rank, b = blockIdx.x, nb = gridDim.x;
+  auto slice_lo = [&](int o) { return count * o / world; };
+  // sub-range of slice o handled by this CTA
+  auto sub = [&](int o, long long& lo, long long& hi) {
+    const long long s0 = slice_lo(o), s1 = slice_lo(o + 1);
+    lo = s0 + (s1 - s0) * b / nb;
+    hi = s0 + (s1 - s0) * (b + 1) / nb;
+  };
+  // 1. push my slice o to owner o's staging row [me]
+  for (int o = 0; o < world; ++o) {
+    long long lo, hi;
+    sub(o, lo, hi);
+    float* stg = reinterpret_cast<float*>(cv.base[o] + cv.L.staging_off) + (size_t)me * count;
+    for (long long i = lo + threadIdx.x; i < hi; i += kArThreads) stg[i - slice_lo(o)] = to_f32(send[i]);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int o = 0; o < world; ++o)
+      st_release_sys(reinterpret_cast<uint32_t*>(cv.base[o] + cv.L.ar_part_off) + (size_t)b * kMaxWorld + me, 1u);
+  // 2. as owner of slice `me`: reduce in rank order, push to everyone
+  if (threadIdx.x == 0) {
+    uint32_t* pf = reinterpret_cast<uint32_t*>(cv.base[me] + cv.L.ar_part_off) + (size_t)b * kMaxWorld;
+    bool ok = true;
+    for (int q = 0; q < world && ok; ++q) ok = wait_flag_sys(pf + q, 1u);
+    if (ok)
+      for (int q = 0; q < world; ++q) pf[q] = 0u;
+    else
+      atomicOr(status, kStatusTimeoutPeer);
+    ok_s = ok;
+  }
+  __syncthreads();
+  {
+    long long lo, hi;
+    sub(me, lo, hi);
+    const size_t row = (size_t)count;
+    const float* stg = reinterpret_cast<const float*>(cv.base[me] + cv.L.staging_off);
+    if (ok_s) {
+      for (long long i = lo + threadIdx.x; i < hi; i += kArThreads) {
+        float acc = 0.f;
+        for (int q = 0; q < world; ++q) acc += __ldcg(stg + (size_t)q * row + (i - slice_lo(me)));
+        const T v = from_f32<T>(acc);
+        for (int q = 0; q < world; ++q) reinterpret_cast<T*>(cv.base[q] + cv.L.result_off)[i] = v;
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && ok_s)
+    for (int q = 0; q < world; ++q)
+      st_release_sys(reinterpret_cast<uint32_t*>(cv.base[q] + cv.L.ar_final_off) + (size_t)me * kArMaxCtas + b, 1u);
+  // 3. collect every owner's result slice into recv
+  for (int o = 0; o < world; ++o) {
+    if (threadIdx.x == 0) {
+      uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[me] + cv.L.ar_final_off) + (size_t)o * kArMaxCtas + b;
+      const bool ok = wait_flag_sys(ff, 1u);
+      if (ok)
+        *ff = 0u;
+      else
+        atomicOr(status, kStatusTimeoutPeer);
+      ok_s = ok;
+    }
+    __syncthreads();
+    long long lo, hi;
+    sub(o, lo, hi);
+    const T* res = reinterpret_cast<const T*>(cv.base[me] + cv.L.result_off);
+    if (ok_s)
+      for (long long i = lo + threadIdx.x; i < hi; i += kArThreads) {
+        T v;
+        if (sizeof(T) == 4) {
+          const float f = __ldcg(reinterpret_cast<const float*>(res) + i);
+          v = from_f32<T>(f);
+        } else {
+          const unsigned short h = __ldcg(reinterpret_cast<const unsigned short*>(res) + i);
+          v = *reinterpret_cast<const T*>(&h);
+        }
+        recv[i] = v;
+      }
+    __syncthreads();
+  }
+}
+
+}  // namespace krt
+
+using namespace krt;
+
+// ------------------------------------------------------------------ C ABI
+extern "C" int krt_comm_create(int32_t rank, int32_t world_size, int32_t max_n_out, krt_comm** out) {
+  if (!out) return set_error(KRT_ERR_INVALID, "krt_comm_create: out is NULL");
+  *out = nullptr;
+  if (world_size < 1 || world_size > kMaxWorld || rank < 0 || rank >= world_size)
+    return set_error(KRT_ERR_INVALID, "krt_comm_create: rank %d / world_size %d outside 1..%d", rank, world_size,
+                     kMaxWorld);
+  if (max_n_out <= 0 || max_n_out % 128 != 0)
+    return set_error(KRT_ERR_INVALID, "krt_comm_create: max_n_out must be a positive multiple of 128");
+  krt_comm* c = new (std::nothrow) krt_comm();
+  if (!c) return set_error(KRT_ERR_INVALID, "krt_comm_create: out of host memory");
+  c->rank = rank;
+  c->world = world_size;
+  c->max_n = max_n_out;
+  c->L = comm_layout(world_size, max_n_out);
+  cudaError_t e = cudaGetDevice(&c->device);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->local), c->L.total);
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->L.total);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    return cuda_error(e, "krt_comm_create");
+  }
+  c->peer[rank] = c->local;
+  if (world_size == 1) c->peers_open = true;
+  *out = c;
+  return clear_error();
+}
+
+extern "C" size_t krt_comm_handle_size(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int krt_comm_ipc_handle(krt_comm* c, void* handle_out) {
+  if (!c || !handle_out) return set_error(KRT_ERR_INVALID, "krt_comm_ipc_handle: NULL argument");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, c->local);
+  if (e != cudaSuccess) return cuda_error(e, "krt_comm_ipc_handle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return clear_error();
+}
+
+extern "C" int krt_comm_open_peers(krt_comm* c, const void* handles) {
+  if (!c || !handles) return set_error(KRT_ERR_INVALID, "krt_comm_open_peers: NULL argument");
+  if (c->peers_open) return clear_error();
+  const char* hp = static_cast<const char*>(handles);
+  for (int q = 0; q < c->world; ++q) {
+    if (q == c->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hp + (size_t)q * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int r = 0; r < q; ++r)
+        if (r != c->rank && c->peer[r]) cudaIpcCloseMemHandle(c->peer[r]), c->peer[r] = nullptr;
+      return cuda_error(e, "krt_comm_open_peers: cudaIpcOpenMemHandle");
+    }
+    c->peer[q] = static_cast<char*>(ptr);
+  }
+  c->peers_open = true;
+  return clear_error();
+}
+
+extern "C" int krt_comm_destroy(krt_comm* c) {
+  if (!c) return clear_error();
+  for (int q = 0; q < c->world; ++q)
+    if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+  return clear_error();
+}
+
+namespace {
+int comm_view(krt_comm* c, CommView* v) {
+  if (!c) return set_error(KRT_ERR_INVALID, "communicator is NULL");
+  if (!c->peers_open) return set_error(KRT_ERR_INVALID, "communicator peers are not open (krt_comm_open_peers)");
+  std::memset(v, 0, sizeof(*v));
+  v->rank = c->rank;
+  v->world = c->world;
+  v->L = c->L;
+  for (int q = 0; q < c->world; ++q) v->base[q] = c->peer[q];
+  return KRT_OK;
+}
+}  // namespace
+
+extern "C" int krt_allreduce(krt_comm* c, const void* send, void* recv, size_t count, int32_t dtype, void* status,
+                             void* stream) {
+  CommView v;
+  int rc = comm_view(c, &v);
+  if (rc) return rc;
+  if (!send || !recv || !status) return set_error(KRT_ERR_INVALID, "krt_allreduce: NULL buffer");
+  if (dtype == 0) dtype = KRT_DTYPE_FLOAT32;  // the mock backend's fp32 code (tests/mock_rccl.h:14)
+  if (dtype != KRT_DTYPE_FLOAT32 && dtype != KRT_DTYPE_BFLOAT16)
+    return set_error(KRT_ERR_UNSUPPORTED, "krt_allreduce: float32 and bfloat16 only");
+  const size_t esize = dtype == KRT_DTYPE_FLOAT32 ? 4 : 2;
+  // Elements per launch: staging holds world rows of (slice + count) floats,
+  // the result area holds count elements.
+  const size_t stg_bytes = v.L.result_off - v.L.staging_off;
+  const size_t res_bytes = v.L.part_flag_off - v.L.result_off;
+  size_t seg = res_bytes / esize;
+  const size_t by_stage = stg_bytes / (sizeof(float) * (size_t)v.world);
+  if (seg > by_stage) seg = by_stage;
+  cudaStream_t s = (cudaStream_t)stream;
+  for (size_t off = 0; off < count; off += seg) {
+    const long long n = (long long)((count - off) < seg ? (count - off) : seg);
+    int ctas = (int)((n + 4095) / 4096);
+    if (ctas < 1) ctas = 1;
+    if (ctas > kArMaxCtas) ctas = kArMaxCtas;
+    if (dtype == KRT_DTYPE_FLOAT32)
+      allreduce_kernel<float><<<ctas, kArThreads, 0, s>>>(static_cast<const float*>(send) + off,
+                                                          static_cast<float*>(recv) + off, n, v,
+                                                          static_cast<int*>(status));
+    else
+      allreduce_kernel<__nv_bfloat16><<<ctas, kArThreads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(send) + off, static_cast<__nv_bfloat16*>(recv) + off, n, v,
+          static_cast<int*>(status));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "krt_allreduce launch");
+  }
+  (void)esize;
+  return clear_error();
+}
+
+// ------------------------------------------------------ fused GEMM + allreduce
+namespace {
+
+int gemm_stages(int n_pad, int kc) {
+  for (int st = kMaxStages; st >= 1; --st)
+    if (gemm_ar_smem_bytes(st, n_pad, kc) <= 227 * 1024) return st;
+  return 0;
+}
+
+int gemm_kc(int num_kb, int n_pad) {
+  int best = 1;
+  size_t best_bytes = 0;
+  for (int kc = 4; kc >= 1; kc >>= 1) {
+    if (num_kb % kc != 0) continue;
+    const size_t bytes = (size_t)gemm_stages(n_pad, kc) * kc * 16384;
+    if (bytes > best_bytes) {
+      best_bytes = bytes;
+      best = kc;
+    }
+  }
+  return best;
+}
+
+int gemm_splits(int tiles, int num_kc, int n_pad, int stages, int kc) {
+  int s = device_sm_count() / tiles;
+  if (s > 8) s = 8;
+  if (s > num_kc) s = num_kc;
+  if (s < 1) s = 1;
+  while (s > 1 && gemm_ar_max_active_clusters(s, n_pad, stages, kc) < tiles) --s;
+  return s;
+}
+
+}  // namespace
+
+extern "C" size_t krt_rowparallel_gemm_ar_workspace_size(void) { return kWsHeaderBytes; }
+
+extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, void* stream) {
+  if (!a) return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: args is NULL");
+  if (!a->x || !a->weight || !a->y) return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: NULL tensor");
+  if (a->num_tokens <= 0 || a->k_local <= 0 || a->n_out <= 0)
+    return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: num_tokens, k_local and n_out must be positive");
+  if (a->k_local % 64 != 0) return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: k_local % 64 != 0");
+  if (a->n_out % 128 != 0) return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: n_out % 128 != 0");
+  if (a->x_stride < a->k_local || a->x_stride % 8 != 0 || a->y_stride < a->n_out || a->y_stride % 8 != 0)
+    return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: strides must cover the rows and be multiples of 8");
+  if ((reinterpret_cast<uintptr_t>(a->x) & 15) || (reinterpret_cast<uintptr_t>(a->weight) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->y) & 15))
+    return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: tensors must be 16-byte aligned");
+  if (!a->workspace || a->workspace_bytes < kWsHeaderBytes)
+    return set_error(KRT_ERR_WORKSPACE, "krt_rowparallel_gemm_ar: workspace of %zu bytes, %zu needed",
+                     a->workspace_bytes, (size_t)kWsHeaderBytes);
+  GemmArParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (c) {
+    int rc = comm_view(c, &p.comm);
+    if (rc) return rc;
+    if (a->n_out > c->max_n)
+      return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: n_out %d exceeds the communicator's %d",
+                       a->n_out, c->max_n);
+  } else {
+    p.comm.world = 1;
+    p.comm.rank = 0;
+  }
+  const int tiles = a->n_out / 128;
+  const int num_kb = a->k_local / 64;
+  p.n_out = a->n_out;
+  p.k_local = a->k_local;
+  p.y_stride = a->y_stride;
+  p.status = static_cast<int*>(a->workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int t0 = 0; t0 < a->num_tokens; t0 += 256) {
+    const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
+    p.num_tokens = T;
+    p.n_pad = (T + 15) / 16 * 16;
+    p.kc = gemm_kc(num_kb, p.n_pad);
+    p.stages = gemm_stages(p.n_pad, p.kc);
+    p.splits = gemm_splits(tiles, num_kb / p.kc, p.n_pad, p.stages, p.kc);
+    int cols = 32;
+    while (cols < p.n_pad) cols <<= 1;
+    p.tmem_cols = cols;
+    p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
+    const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
+    CUtensorMap tmap_w, tmap_x;
+    int rc = make_tmap_bf16_3d(&tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local, (uint64_t)a->k_local,
+                               128, (uint32_t)p.kc);
+    if (rc) return rc;
+    rc = make_tmap_bf16_3d(&tmap_x, xp, (uint64_t)T, (uint64_t)a->k_local, (uint64_t)a->x_stride, (uint32_t)p.n_pad,
+                           (uint32_t)p.kc);
+    if (rc) return rc;
+    cudaError_t e = launch_rowparallel_gemm_ar(tmap_w, tmap_x, p, tiles, s);
+    if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
+  }
+  return clear_error();
+}

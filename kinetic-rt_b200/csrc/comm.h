@@ -1,0 +1,65 @@
+// Symmetric peer buffers shared by the fused row-parallel GEMM + allreduce
+// and the standalone allreduce.
+//
+// Every rank allocates one device buffer with the same layout, exports it as
+// a CUDA IPC handle, and maps every peer's buffer into its own address space
+// (krt_comm_open_peers).  Kernels then write partial sums and flags straight
+// into peers' buffers over NVLink / NVSwitch with ordinary stores; no TMA or
+// multicast load ever reads peer memory.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_bf16.h>
+
+namespace krt {
+
+constexpr int kMaxWorld = 8;
+constexpr int kArMaxCtas = 64;     // CTAs of the standalone allreduce
+constexpr int kChunkTokens = 16;   // token granularity of the fused exchange
+constexpr int kMaxChunks = 16;     // 256 tokens per launch
+
+struct CommLayout {
+  int world, max_n, tiles;
+  size_t staging_off;      // fp32 [world][tiles][kMaxChunks][16 * 128]
+  size_t result_off;       // [256][max_n] bf16 (fused) / raw bytes (standalone)
+  size_t part_flag_off;    // u32 [tiles][kMaxChunks][kMaxWorld]
+  size_t final_flag_off;   // u32 [tiles][kMaxChunks]
+  size_t ar_part_off;      // u32 [kArMaxCtas][kMaxWorld]
+  size_t ar_final_off;     // u32 [kMaxWorld][kArMaxCtas]
+  size_t total;
+};
+
+inline CommLayout comm_layout(int world, int max_n) {
+  auto up = [](size_t v) { return (v + 4095) & ~size_t(4095); };
+  CommLayout L;
+  L.world = world;
+  L.max_n = max_n;
+  L.tiles = max_n / 128;
+  L.staging_off = 0;
+  L.result_off = up(L.staging_off + (size_t)world * L.tiles * kMaxChunks * 16 * 128 * sizeof(float));
+  L.part_flag_off = up(L.result_off + (size_t)kMaxChunks * 16 * max_n * 2);
+  L.final_flag_off = up(L.part_flag_off + (size_t)L.tiles * kMaxChunks * kMaxWorld * 4);
+  L.ar_part_off = up(L.final_flag_off + (size_t)L.tiles * kMaxChunks * 4);
+  L.ar_final_off = up(L.ar_part_off + (size_t)kArMaxCtas * kMaxWorld * 4);
+  L.total = up(L.ar_final_off + (size_t)kMaxWorld * kArMaxCtas * 4);
+  return L;
+}
+
+// Device-side view of a communicator: each rank's buffer as mapped here.
+struct CommView {
+  int rank, world;
+  char* base[kMaxWorld];
+  CommLayout L;
+};
+
+// Launch parameters of the fused row-parallel GEMM + allreduce (gemm_ar.cu).
+struct GemmArParams {
+  __nv_bfloat16* y;
+  int y_stride;
+  int num_tokens, n_pad, n_out, k_local;
+  int splits, stages, kc, tmem_cols;
+  int* status;
+  CommView comm;
+};
+
+}  // namespace krt

@@ -257,6 +257,29 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
   return v;
 }
 
+// ------------------------------------------------------- cross-GPU flags
+// Flags live in symmetric buffers that peers write over NVLink.  A producer
+// fences its data stores system-wide, then releases the flag; the consumer
+// acquires it.  Waits are bounded by kWaitBudgetNs.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until *flag == expect; false after kWaitBudgetNs.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t expect) {
+  if (ld_acquire_sys(flag) == expect) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (ld_acquire_sys(flag) == expect) return true;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+    __nanosleep(64);
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

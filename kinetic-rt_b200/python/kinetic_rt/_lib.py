@@ -53,6 +53,15 @@ class QkvPagedArgs(ctypes.Structure):
     ]
 
 
+class GemmArArgs(ctypes.Structure):
+    """krt_gemm_ar_args"""
+    _fields_ = [
+        ("x", _vp), ("weight", _vp), ("y", _vp),
+        ("num_tokens", _i32), ("k_local", _i32), ("n_out", _i32), ("x_stride", _i32), ("y_stride", _i32),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 # Every symbol include/krt.h declares, with (restype, argtypes).
 SIGNATURES = {
     "krt_last_error": (ctypes.c_char_p, []),
@@ -63,6 +72,14 @@ SIGNATURES = {
     "krt_qkv_rope_prefill_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     "krt_qkv_rope_prefill": (ctypes.c_int, [ctypes.POINTER(QkvPagedArgs), _vp]),
     "krt_read_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i32)]),
+    "krt_comm_create": (ctypes.c_int, [_i32, _i32, _i32, ctypes.POINTER(_vp)]),
+    "krt_comm_handle_size": (ctypes.c_size_t, []),
+    "krt_comm_ipc_handle": (ctypes.c_int, [_vp, _vp]),
+    "krt_comm_open_peers": (ctypes.c_int, [_vp, _vp]),
+    "krt_comm_destroy": (ctypes.c_int, [_vp]),
+    "krt_allreduce": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t, _i32, _vp, _vp]),
+    "krt_rowparallel_gemm_ar_workspace_size": (ctypes.c_size_t, []),
+    "krt_rowparallel_gemm_ar": (ctypes.c_int, [_vp, ctypes.POINTER(GemmArArgs), _vp]),
 }
 
 _lib = None
@@ -182,3 +199,51 @@ def read_status(workspace, stream=None):
     bits = _i32(0)
     rc = lib().krt_read_status(_ptr(workspace), _stream(stream), ctypes.byref(bits))
     return rc, bits.value
+
+
+# ------------------------------------------------------------ communicator
+def comm_create(rank, world_size, max_n_out):
+    h = _vp()
+    check(lib().krt_comm_create(int(rank), int(world_size), int(max_n_out), ctypes.byref(h)))
+    return h
+
+
+def comm_ipc_handle(comm):
+    n = int(lib().krt_comm_handle_size())
+    buf = ctypes.create_string_buffer(n)
+    check(lib().krt_comm_ipc_handle(comm, buf))
+    return buf.raw
+
+
+def comm_open_peers(comm, handles):
+    blob = b"".join(handles)
+    check(lib().krt_comm_open_peers(comm, ctypes.c_char_p(blob)))
+
+
+def comm_destroy(comm):
+    if comm:
+        check(lib().krt_comm_destroy(comm))
+
+
+def allreduce(comm, send, recv, status, stream=None):
+    check(lib().krt_allreduce(comm, _ptr(send), _ptr(recv), int(send.numel()), _dtype_code(send), _ptr(status),
+                              _stream(stream)))
+
+
+def gemm_ar_workspace_bytes():
+    return int(lib().krt_rowparallel_gemm_ar_workspace_size())
+
+
+def gemm_ar_args(x, weight, y, workspace):
+    a = GemmArArgs()
+    a.x, a.weight, a.y = _ptr(x), _ptr(weight), _ptr(y)
+    a.num_tokens, a.k_local = int(x.shape[0]), int(x.shape[1])
+    a.n_out = int(weight.shape[0])
+    a.x_stride, a.y_stride = int(x.stride(0)), int(y.stride(0))
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel() * workspace.element_size()
+    return a
+
+
+def rowparallel_gemm_ar(comm, args, stream=None):
+    check(lib().krt_rowparallel_gemm_ar(comm, ctypes.byref(args), _stream(stream)))
