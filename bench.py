@@ -1,0 +1,424 @@
+"""Benchmark of the decoder hot path on B200.
+
+One step = one Llama-3-8B decoder layer's hot path for a decode batch of 64
+sequences at context 2048, tensor-parallel over N GPUs (one process each):
+
+  1. fused RMSNorm + QKV projection + RoPE + paged K/V scatter
+     (krt_qkv_rope_decode; Q/K/V heads split over ranks, no collective)
+  2. o_proj   row-parallel GEMM fused with the allreduce (K = 4096 / N)
+  3. down_proj row-parallel GEMM fused with the allreduce (K = 14336 / N)
+
+Inputs are synthetic (seeded N(0,1) activations, N(0, 0.02) weights,
+gamma = 1 + N(0, 0.1), block tables a seeded permutation of the pool).  Each
+step uses the weights of a different layer, cycling over enough layers that
+the weights touched between two uses of a layer exceed the 126 MB L2.
+Steps are CUDA-graph replays; the timed region is bracketed by a barrier and
+device synchronisation and timed with CUDA events, max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl krt|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run.  Prints one
+JSON line on rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "kinetic-rt_b200"))
+
+METRIC = "decode tokens/s per box at TP=1/2/4/8; fused QKV+RoPE & GEMM+AR % roofline"
+HIDDEN, N_HEADS, N_KV, HEAD_DIM, INTER = 4096, 32, 8, 128, 14336
+BATCH, CTX, BLOCK = 64, 2048, 16
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def workload_config(n):
+    return {
+        "workload": (f"Llama-3-8B decoder-layer hot path, decode batch {BATCH} at context {CTX}, TP={n}: "
+                     "fused RMSNorm+QKV+RoPE+paged-KV scatter, o_proj GEMM+allreduce, down_proj GEMM+allreduce"),
+        "global_batch": BATCH, "seq_len": CTX, "parallelism": f"tp{n}", "hidden": HIDDEN,
+        "heads": f"{N_HEADS}/{N_KV}x{HEAD_DIM}", "intermediate": INTER, "kv_block": BLOCK,
+        "l2": "weights rotated over layers whose total exceeds L2",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """SM clocks and clock-event (throttle) reasons sampled through NVML every
+    2 ms while the timed region runs."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
+
+    def __init__(self, gpu_index):
+        self.gpu, self.samples, self.reasons, self.stop_evt, self.thread = gpu_index, [], set(), None, None
+        self.max_mhz = None
+
+    def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            return
+        self.stop_evt = threading.Event()
+
+        def poll():
+            while not self.stop_evt.is_set():
+                try:
+                    self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for mask, name in self.REASONS.items():
+                        if bits & mask:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0, "reasons": ["nvml unavailable"]}
+        self.stop_evt.set()
+        self.thread.join(timeout=2)
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples), "reasons": sorted(self.reasons)}
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_baseline(seconds=10.0):
+    """The reference's CPU path (torch fp32 on all host cores, oracle/torch_ref.py)
+    on the full step's shapes, repeated for about `seconds`."""
+    import torch
+    from oracle import torch_ref
+    from oracle.fused_layer import rope_tables
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(BATCH, HIDDEN, generator=g)
+    w_qkv = torch.randn((N_HEADS + 2 * N_KV) * HEAD_DIM, HIDDEN, generator=g) * 0.02
+    gamma = 1 + 0.1 * torch.randn(HIDDEN, generator=g)
+    cos, sin = (torch.from_numpy(a) for a in rope_tables([CTX - 1] * BATCH, HEAD_DIM, 5e5))
+    attn = torch.randn(BATCH, HIDDEN, generator=g)
+    w_o = torch.randn(HIDDEN, HIDDEN, generator=g) * 0.02
+    act = torch.randn(BATCH, INTER, generator=g)
+    w_d = torch.randn(HIDDEN, INTER, generator=g) * 0.02
+    torch_ref.layer_hot_path_ref(x, w_qkv, gamma, cos, sin, attn, w_o, act, w_d, N_HEADS, N_KV, HEAD_DIM)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        torch_ref.layer_hot_path_ref(x, w_qkv, gamma, cos, sin, attn, w_o, act, w_d, N_HEADS, N_KV, HEAD_DIM)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": BATCH / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} steps of the full {BATCH}-token layer hot path in torch fp32 (oracle/torch_ref.py), "
+                      f"{dt * 1e3:.1f} ms/step"}
+
+
+# --------------------------------------------------------------- GPU setup
+class Layer:
+    """Weights of one decoder layer (this rank's shards)."""
+
+    def __init__(self, torch, rank, world, seed):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        hq, hkv = N_HEADS // world, N_KV // world
+        rows = (hq + 2 * hkv) * HEAD_DIM
+        self.w_qkv = (torch.randn(rows, HIDDEN, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        self.gamma = (1 + 0.1 * torch.randn(HIDDEN, generator=g, device="cuda")).to(torch.bfloat16)
+        self.w_o = (torch.randn(HIDDEN, HIDDEN // world, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        self.w_d = (torch.randn(HIDDEN, INTER // world, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+
+    @property
+    def nbytes(self):
+        return sum(t.numel() * 2 for t in (self.w_qkv, self.gamma, self.w_o, self.w_d))
+
+
+class Rig:
+    def __init__(self, torch, rank, world, comm):
+        from python.kinetic_rt import _lib
+        from oracle.fused_layer import rope_tables
+        self.torch, self.lib, self.rank, self.world, self.comm = torch, _lib, rank, world, comm
+        self.hq, self.hkv = N_HEADS // world, N_KV // world
+        g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+        probe = Layer(torch, rank, world, 0)
+        self.n_layers = max(2, -(-2 * L2_BYTES // probe.nbytes) + 1)
+        self.layers = [probe] + [Layer(torch, rank, world, 1 + i) for i in range(self.n_layers - 1)]
+        self.x = torch.randn(BATCH, HIDDEN, generator=g, device="cuda").to(torch.bfloat16)
+        self.attn = torch.randn(BATCH, HIDDEN // world, generator=g, device="cuda").to(torch.bfloat16)
+        self.act = torch.randn(BATCH, INTER // world, generator=g, device="cuda").to(torch.bfloat16)
+        cos, sin = rope_tables(range(CTX), HEAD_DIM, 5e5)
+        self.cos, self.sin = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+        self.positions = torch.full((BATCH,), CTX - 1, dtype=torch.int32, device="cuda")
+        self.token_seq = torch.arange(BATCH, dtype=torch.int32, device="cuda")
+        blocks_per_seq = CTX // BLOCK
+        self.num_blocks = BATCH * blocks_per_seq
+        perm = torch.randperm(self.num_blocks, generator=torch.Generator().manual_seed(7)).to(torch.int32)
+        self.block_table = perm.view(BATCH, blocks_per_seq).cuda()
+        self.pool = torch.zeros(self.num_blocks, BLOCK, 2 * self.hkv * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+        self.q = torch.empty(BATCH, self.hq * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+        self.y_o = torch.empty(BATCH, HIDDEN, dtype=torch.bfloat16, device="cuda")
+        self.y_d = torch.empty(BATCH, HIDDEN, dtype=torch.bfloat16, device="cuda")
+        self.ws_qkv = torch.zeros(_lib.decode_workspace_bytes(BATCH, HIDDEN, self.hq, self.hkv), dtype=torch.uint8,
+                                  device="cuda")
+        self.ws_gemm = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+        self.args = []
+        for L in self.layers:
+            qa = _lib.paged_args(self.x, L.w_qkv, None, L.gamma, self.cos, self.sin, self.positions, self.token_seq,
+                                 self.block_table, self.pool, self.q, self.hq, self.hkv, self.num_blocks, BLOCK,
+                                 self.ws_qkv)
+            oa = _lib.gemm_ar_args(self.attn, L.w_o, self.y_o, self.ws_gemm)
+            da = _lib.gemm_ar_args(self.act, L.w_d, self.y_d, self.ws_gemm)
+            self.args.append((qa, oa, da))
+        self.comm_handle = comm.handle if comm is not None else None
+        self.launches_per_step = 4  # prep + decode, o_proj, down_proj
+
+    def step(self, i, parts=(0, 1, 2)):
+        qa, oa, da = self.args[i % self.n_layers]
+        if 0 in parts:
+            self.lib.qkv_rope_decode(qa)
+        if 1 in parts:
+            self.lib.rowparallel_gemm_ar(self.comm_handle, oa)
+        if 2 in parts:
+            self.lib.rowparallel_gemm_ar(self.comm_handle, da)
+
+    def graphs(self, parts=(0, 1, 2)):
+        torch = self.torch
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for i in range(self.n_layers):
+                self.step(i, parts)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        gs = []
+        for i in range(self.n_layers):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.step(i, parts)
+            gs.append(g)
+        return gs
+
+    def check_status(self):
+        for ws in (self.ws_qkv, self.ws_gemm):
+            rc, bits = self.lib.read_status(ws)
+            if rc != 0:
+                raise RuntimeError(f"kernel status {bits:#x}")
+
+
+def max_over_ranks(torch, value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(torch, world):
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def timed_graph_replays(torch, graphs, steps, world):
+    barrier(torch, world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        graphs[i % len(graphs)].replay()
+    b.record()
+    barrier(torch, world)
+    return a.elapsed_time(b)  # ms
+
+
+def run_krt(args, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    comm = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=120))
+        from python.kinetic_rt.dist import TPComm
+        comm = TPComm(rank, world, max_n_out=HIDDEN)
+    rig = Rig(torch, rank, world, comm)
+    graphs = rig.graphs()
+    for i in range(args.warmup):
+        graphs[i % len(graphs)].replay()
+    rig.check_status()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.05)
+    ms = timed_graph_replays(torch, graphs, args.steps, world)
+    clk = clocks.stop()
+    rig.check_status()
+    ms = max_over_ranks(torch, ms, world)
+    ms_step = ms / args.steps
+    value = BATCH / (ms_step * 1e-3)
+
+    # per-kernel durations: graphs of one kernel type, replayed over all layers
+    hbm, peak_kind = peaks()
+    kernels = []
+    hq, hkv = rig.hq, rig.hkv
+    kbytes = [
+        ("qkv_rope_decode", (hq + 2 * hkv) * HEAD_DIM * HIDDEN * 2 + BATCH * HIDDEN * 2 * 2 + BATCH * hkv * HEAD_DIM * 4,
+         "W_qkv + x read, q + K/V written"),
+        ("o_proj_gemm_ar", HIDDEN * (HIDDEN // world) * 2 + BATCH * (HIDDEN // world) * 2 + BATCH * HIDDEN * 2,
+         "W_o shard + x read, y written"),
+        ("down_proj_gemm_ar", HIDDEN * (INTER // world) * 2 + BATCH * (INTER // world) * 2 + BATCH * HIDDEN * 2,
+         "W_down shard + x read, y written"),
+    ]
+    traffic = {}
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            traffic = json.load(f)
+    except Exception:
+        pass
+    reps = max(min(args.steps, 2000), 2 * rig.n_layers)
+    for part, (name, nbytes, what) in enumerate(kbytes):
+        g = rig.graphs(parts=(part,))
+        for i in range(3):
+            g[i % len(g)].replay()
+        kms = max_over_ranks(torch, timed_graph_replays(torch, g, reps, world), world) / reps
+        ach = nbytes / (kms * 1e-3) / 1e9
+        kernels.append({"kernel": name, "bound": "hbm", "us": round(kms * 1e3, 3), "algorithmic_bytes": nbytes,
+                        "bytes": what, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(ach / hbm, 4), "traffic": traffic.get(f"{name}_tp{world}")})
+    rig.check_status()
+    dominant = max(kernels, key=lambda k: k["us"])
+
+    # end to end through the C ABI with host buffers: H2D of the step's
+    # activations, the three calls, D2H of q and both layer outputs
+    pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())
+    hx, hattn, hact = pin(rig.x), pin(rig.attn), pin(rig.act)
+    hq_out, hyo, hyd = (torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (rig.q, rig.y_o, rig.y_d))
+    h2d = sum(t.numel() * t.element_size() for t in (hx, hattn, hact))
+    d2h = sum(t.numel() * t.element_size() for t in (hq_out, hyo, hyd))
+    e2e_steps = max(4, min(args.steps, 50))
+    for i in range(2):
+        rig.step(i)
+    barrier(torch, world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(e2e_steps):
+        rig.x.copy_(hx, non_blocking=True)
+        rig.attn.copy_(hattn, non_blocking=True)
+        rig.act.copy_(hact, non_blocking=True)
+        rig.step(i)
+        hq_out.copy_(rig.q, non_blocking=True)
+        hyo.copy_(rig.y_o, non_blocking=True)
+        hyd.copy_(rig.y_d, non_blocking=True)
+    b.record()
+    barrier(torch, world)
+    e2e_ms = max_over_ranks(torch, a.elapsed_time(b), world) / e2e_steps
+    rig.check_status()
+
+    base = cpu_baseline() if rank == 0 else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s (one decoder layer's hot path)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random weights and activations)", "config": workload_config(world),
+            "e2e": {"value": round(BATCH / (e2e_ms * 1e-3), 1), "unit": "tokens/s (one decoder layer's hot path)",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": rig.launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "kernel": dominant["kernel"], "achieved": dominant["achieved"],
+                         "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["frac"],
+                         "traffic": dominant["traffic"]},
+            "kernels": kernels,
+            "cpu_baseline": base,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        import torch.distributed as dist
+        del graphs
+        torch.cuda.synchronize()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args, rank, world):
+    """The reference's own CPU path (torch fp32, every host core), rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import torch_ref
+    from oracle.fused_layer import rope_tables
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(BATCH, HIDDEN, generator=g)
+    w_qkv = torch.randn((N_HEADS + 2 * N_KV) * HEAD_DIM, HIDDEN, generator=g) * 0.02
+    gamma = 1 + 0.1 * torch.randn(HIDDEN, generator=g)
+    cos, sin = (torch.from_numpy(a) for a in rope_tables([CTX - 1] * BATCH, HEAD_DIM, 5e5))
+    attn = torch.randn(BATCH, HIDDEN, generator=g)
+    w_o = torch.randn(HIDDEN, HIDDEN, generator=g) * 0.02
+    act = torch.randn(BATCH, INTER, generator=g)
+    w_d = torch.randn(HIDDEN, INTER, generator=g) * 0.02
+    f = lambda: torch_ref.layer_hot_path_ref(x, w_qkv, gamma, cos, sin, attn, w_o, act, w_d, N_HEADS, N_KV, HEAD_DIM)
+    # Each step is ~10 ms of CPU work: run at most 2000 so the arm ends in minutes.
+    steps, warmup = min(args.steps, 2000), min(args.warmup, 10)
+    for _ in range(warmup):
+        f()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        f()
+    dt = (time.perf_counter() - t0) / steps
+    value = BATCH / dt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 1),
+        "unit": "tokens/s (one decoder layer's hot path)", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and activations)",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{steps} steps of the full {BATCH}-token layer hot path in torch fp32 "
+                                   "(oracle/torch_ref.py restating tests/test_fusion.py:11-51)"},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s (one decoder layer's hot path)",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["krt", "reference"], default="krt")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}; using WORLD_SIZE", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_krt(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

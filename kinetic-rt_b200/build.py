@@ -134,9 +134,10 @@ def build_all(jobs=8, only=None):
         outs.append(build_lib(jobs))
     if only in (None, "cubin"):
         outs.append(build_cubin())
-    if only in (None, "core"):
+    have_runtime = os.path.exists(os.path.join(CSRC, "bindings", "python_bindings.cpp"))
+    if only in (None, "core") and have_runtime:
         outs.append(build_core(False, jobs))
-    if only in (None, "mock"):
+    if only in (None, "mock") and have_runtime:
         outs.append(build_core(True, jobs))
     return outs
 
