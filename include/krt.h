@@ -152,6 +152,24 @@ KRT_API size_t krt_qkv_rope_prefill_workspace_size(int32_t num_tokens, int32_t d
                                            int32_t n_kv_heads, int32_t head_dim);
 KRT_API int krt_qkv_rope_prefill(const krt_qkv_paged_args* args, void* stream);
 
+/* Decode for callers that cannot allocate device memory.  No counterpart in
+ * the reference.  Same computation and arguments as krt_qkv_rope_decode, but
+ * args->workspace / workspace_bytes are ignored: the workspace is a fixed
+ * 4 MiB array in the library's own device memory, reserved on every GPU that
+ * loads the library until the process exits.  Meant for callers whose device
+ * memory is owned by someone else (a host application's allocator that forbids
+ * outside cudaMalloc) or that must not allocate after start-up.
+ *  - Calls whose workspace would exceed 4 MiB (krt_qkv_rope_decode_workspace_size)
+ *    are rejected with KRT_ERR_UNSUPPORTED.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture on the device.
+ *  - Every call on a device shares the one array and clears its header at the
+ *    start; calls that can overlap on the GPU (different streams without
+ *    ordering) race on it.  The status word is not readable by the caller.
+ *  - Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+KRT_API int krt_qkv_rope_decode_noalloc(const krt_qkv_paged_args* args, void* stream);
+
 /* Copy the device status word of a workspace to the host (synchronises the
  * stream), clear it, and return KRT_OK or KRT_ERR_DEVICE with the bits in
  * *bits. */
