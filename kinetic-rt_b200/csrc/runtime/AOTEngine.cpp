@@ -1,0 +1,376 @@
+// .kin serializer and AOT engine (interface of the reference's
+// src/AOTEngine.cpp:64-598, behaviour and error messages kept so existing
+// callers and tests see the same contract).
+#include "AOTEngine.h"
+
+#include <dlfcn.h>
+#include <endian.h>
+
+#include <algorithm>
+#include <cctype>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+
+#if !defined(KRT_MOCK_CUDA)
+#include "krt.h"
+#endif
+
+namespace {
+
+std::string env_or_empty(const char* name) {
+  const char* v = std::getenv(name);
+  return v ? std::string(v) : std::string();
+}
+
+// Value of "artifact_kind" in the JSON op-graph metadata, or "" if absent.
+std::string artifact_kind_of(const std::vector<uint8_t>& meta) {
+  const std::string s(meta.begin(), meta.end());
+  const std::string key = "\"artifact_kind\"";
+  size_t p = s.find(key);
+  if (p == std::string::npos) return "";
+  p = s.find(':', p + key.size());
+  if (p == std::string::npos) return "";
+  p = s.find('"', p + 1);
+  if (p == std::string::npos) return "";
+  const size_t e = s.find('"', p + 1);
+  return e == std::string::npos ? "" : s.substr(p + 1, e - p - 1);
+}
+
+std::string read_header(std::ifstream& in, const std::string& filepath, KinHeader* h, std::streamsize* size) {
+  (void)filepath;
+  in.seekg(0, std::ios::end);
+  *size = in.tellg();
+  in.seekg(0, std::ios::beg);
+  if (*size < static_cast<std::streamsize>(sizeof(KinHeader)))
+    throw std::runtime_error("Invalid file format: file too small for header.");
+  in.read(reinterpret_cast<char*>(h), sizeof(KinHeader));
+  if (le32toh(h->magic_number) != kKinMagic) throw std::runtime_error("Invalid file format: bad magic number.");
+  return std::string();
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- Serializer
+Serializer::Serializer() {
+  const std::string forced = env_or_empty("KINETIC_TARGET");
+  if (!forced.empty()) {
+    device_id_ = forced;
+    return;
+  }
+#if defined(KRT_MOCK_CUDA)
+  device_id_ = "CPU";
+#else
+  cudaDeviceProp prop;
+  KRT_CHECK_CUDA(cudaGetDeviceProperties(&prop, 0));
+  device_id_ = "sm" + std::to_string(prop.major) + std::to_string(prop.minor);
+#endif
+}
+
+void Serializer::save_kin_file(const std::string& filepath, const std::string& device_id,
+                               const std::string& kinetic_target, uint64_t weights_hash,
+                               const std::vector<uint8_t>& op_graph_data, const std::vector<uint8_t>& kernel_binaries) {
+  std::ofstream out(filepath, std::ios::binary);
+  if (!out) throw std::runtime_error("Failed to open file for writing: " + filepath);
+  KinHeader h;
+  std::memset(&h, 0, sizeof(h));
+  h.magic_number = htole32(kKinMagic);
+  h.version = htole32(1);
+  std::strncpy(h.device_id, device_id.c_str(), sizeof(h.device_id) - 1);
+  std::strncpy(h.kinetic_target, kinetic_target.c_str(), sizeof(h.kinetic_target) - 1);
+  h.weights_hash = htole64(weights_hash);
+  h.op_graph_data_offset = htole64(sizeof(KinHeader));
+  h.op_graph_data_size = htole64(op_graph_data.size());
+  h.kernel_binaries_offset = htole64(sizeof(KinHeader) + op_graph_data.size());
+  h.kernel_binaries_size = htole64(kernel_binaries.size());
+  h.tensor_parallel_degree = htole32(1);
+  out.write(reinterpret_cast<const char*>(&h), sizeof(h));
+  out.write(reinterpret_cast<const char*>(op_graph_data.data()), op_graph_data.size());
+  out.write(reinterpret_cast<const char*>(kernel_binaries.data()), kernel_binaries.size());
+  if (!out) throw std::runtime_error("Failed to write file: " + filepath);
+}
+
+std::vector<uint8_t> Serializer::load_kin_file(const std::string& filepath) {
+  std::ifstream in(filepath, std::ios::binary);
+  if (!in) throw std::runtime_error("Failed to open file for reading: " + filepath);
+  KinHeader h;
+  std::streamsize size = 0;
+  read_header(in, filepath, &h, &size);
+  const uint64_t og_off = le64toh(h.op_graph_data_offset), og_size = le64toh(h.op_graph_data_size);
+  const uint64_t kb_off = le64toh(h.kernel_binaries_offset), kb_size = le64toh(h.kernel_binaries_size);
+  if (og_off + og_size < og_off || kb_off + kb_size < kb_off)
+    throw std::runtime_error("Invalid file format: offset overflow.");
+  if (og_off + og_size > static_cast<uint64_t>(size) || kb_off + kb_size > static_cast<uint64_t>(size))
+    throw std::runtime_error("Invalid file format: sizes exceed file bounds.");
+  h.device_id[sizeof(h.device_id) - 1] = '\0';
+  h.kinetic_target[sizeof(h.kinetic_target) - 1] = '\0';
+  loaded_kinetic_target_ = h.kinetic_target;
+  if (device_id_ != h.device_id)
+    throw HardwareMismatchError("Hardware mismatch: expected Kinetic target " + std::string(h.device_id) +
+                                " but got " + device_id_);
+  std::vector<uint8_t> bin(kb_size);
+  in.seekg(static_cast<std::streamoff>(kb_off), std::ios::beg);
+  in.read(reinterpret_cast<char*>(bin.data()), static_cast<std::streamsize>(kb_size));
+  if (in.gcount() != static_cast<std::streamsize>(kb_size))
+    throw std::runtime_error("Invalid file format: short read on kernel binaries.");
+  return bin;
+}
+
+uint32_t Serializer::get_tensor_parallel_degree(const std::string& filepath) {
+  std::ifstream in(filepath, std::ios::binary);
+  if (!in) throw std::runtime_error("Failed to open file for reading: " + filepath);
+  KinHeader h;
+  std::streamsize size = 0;
+  read_header(in, filepath, &h, &size);
+  return le32toh(h.tensor_parallel_degree);
+}
+
+// ----------------------------------------------------------------- AOTEngine
+AOTEngine::AOTEngine() = default;
+
+AOTEngine::~AOTEngine() {
+  if (library_) cudaLibraryUnload(library_);
+  library_ = nullptr;
+}
+
+uint64_t AOTEngine::compute_fnv1a_hash(const std::vector<uint8_t>& data) {
+  uint64_t h = 0xcbf29ce484222325ull;
+  for (uint8_t b : data) {
+    h ^= b;
+    h *= 0x100000001b3ull;
+  }
+  return h;
+}
+
+std::string AOTEngine::kernel_dir() {
+  Dl_info info;
+  if (dladdr(reinterpret_cast<void*>(&AOTEngine::compute_fnv1a_hash), &info) && info.dli_fname) {
+    std::string p(info.dli_fname);
+    const size_t slash = p.rfind('/');
+    return (slash == std::string::npos ? std::string(".") : p.substr(0, slash)) + "/kernels";
+  }
+  return "kernels";
+}
+
+void AOTEngine::compile_ahead_of_time(const std::string& output_filepath, uintptr_t stream_ptr,
+                                      const std::string& kinetic_target) {
+  (void)stream_ptr;
+  std::lock_guard<std::recursive_mutex> lock(mutex_);
+  const std::string path = kernel_dir() + "/fused_rmsnorm_qkv_rope.sm_100a.cubin";
+  std::ifstream in(path, std::ios::binary);
+  if (!in) throw std::runtime_error("AOT compilation failed: kernel image not found at " + path);
+  std::vector<uint8_t> binary((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+#if defined(KRT_MOCK_CUDA)
+  const char* kind = "mock";
+#else
+  const char* kind = "production";
+#endif
+  const std::string meta = std::string("{\"target\": \"") + kinetic_target +
+                           "\", \"kernels\": [\"fused_rmsnorm_qkv_rope\", \"fused_rmsnorm_qkv_rope_bf16\"], "
+                           "\"version\": 1, \"artifact_kind\": \"" + kind + "\"}";
+  serializer_.save_kin_file(output_filepath, serializer_.get_device_id(), kinetic_target,
+                            compute_fnv1a_hash(binary), std::vector<uint8_t>(meta.begin(), meta.end()), binary);
+}
+
+void AOTEngine::load_model(const std::string& filepath) {
+  std::lock_guard<std::recursive_mutex> lock(mutex_);
+  std::ifstream in(filepath, std::ios::binary);
+  if (!in) throw std::runtime_error("Failed to open file for reading: " + filepath);
+  KinHeader h;
+  std::streamsize size = 0;
+  read_header(in, filepath, &h, &size);
+  const uint64_t off = le64toh(h.op_graph_data_offset), len = le64toh(h.op_graph_data_size);
+  if (off + len < off || off + len > static_cast<uint64_t>(size))
+    throw std::runtime_error("Invalid file format: op_graph_data exceeds file bounds.");
+  std::vector<uint8_t> meta(len);
+  in.seekg(static_cast<std::streamoff>(off), std::ios::beg);
+  in.read(reinterpret_cast<char*>(meta.data()), static_cast<std::streamsize>(len));
+  if (in.gcount() != static_cast<std::streamsize>(len))
+    throw std::runtime_error("Invalid file format: short read on metadata.");
+  std::string kind = artifact_kind_of(meta);
+  if (kind.empty()) kind = "mock";  // unverified artifacts are treated as mocks
+  if (kind == "mock" && env_or_empty("KINETIC_ALLOW_MOCKS") != "1")
+    throw std::runtime_error(
+        "FATAL: Refusing to load mock artifact in production mode. "
+        "To override this safeguard for testing, export KINETIC_ALLOW_MOCKS=1.");
+  std::vector<uint8_t> binary = serializer_.load_kin_file(filepath);
+  load_kernel(binary, serializer_.get_loaded_kinetic_target());
+}
+
+void AOTEngine::validate_elf_structure(const std::vector<uint8_t>& b, const std::string& target) const {
+  if (b.size() < 64) throw std::runtime_error("Cannot load kernel: binary data too small for a valid ELF header.");
+  if (b[0] != 0x7f || b[1] != 'E' || b[2] != 'L' || b[3] != 'F')
+    throw std::runtime_error("Cannot load kernel: invalid or missing ELF header.");
+  if (b[4] != 2) throw std::runtime_error("Cannot load kernel: ELF binary is not 64-bit.");
+  const uint16_t machine = static_cast<uint16_t>(b[18] | (b[19] << 8));
+  const bool cuda = target.rfind("CUDA", 0) == 0 || target.find("sm") != std::string::npos;
+  if (target != serializer_.get_loaded_kinetic_target())
+    throw HardwareMismatchError("Hardware mismatch: expected Kinetic target string mismatch.");
+  if (machine != (cuda ? 0xBE : 0xE0))
+    throw std::runtime_error("Cannot load kernel: ELF binary architecture mismatch for current platform.");
+}
+
+void AOTEngine::load_kernel(const std::vector<uint8_t>& binary, const std::string& target) {
+  std::lock_guard<std::recursive_mutex> lock(mutex_);
+  validate_elf_structure(binary, target);
+  if (library_) {
+    cudaLibraryUnload(library_);
+    library_ = nullptr;
+  }
+  kernels_.clear();
+  default_kernel_name_.clear();
+  KRT_CHECK_CUDA(cudaLibraryLoadData(&library_, binary.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
+  std::vector<std::string> names;
+  const std::string env = env_or_empty("KINETIC_KERNEL_SYMBOLS");
+  if (!env.empty()) {
+    std::stringstream ss(env);
+    std::string item;
+    while (std::getline(ss, item, ',')) {
+      item.erase(std::remove_if(item.begin(), item.end(), [](unsigned char c) { return std::isspace(c); }),
+                 item.end());
+      if (!item.empty()) names.push_back(item);
+    }
+  }
+  if (names.empty())
+    names = {"fused_rmsnorm_qkv_rope", "fused_rmsnorm_qkv_rope_bf16", "kernel", "triton_kernel", "fused_kernel",
+             "matmul_kernel", "main"};
+  for (const auto& n : names) {
+    cudaKernel_t k = nullptr;
+    if (cudaLibraryGetKernel(&k, library_, n.c_str()) == cudaSuccess && k) {
+      kernels_[n] = k;
+      if (default_kernel_name_.empty()) default_kernel_name_ = n;
+    } else {
+      cudaGetLastError();
+    }
+  }
+  if (kernels_.empty())
+    throw std::runtime_error("Cannot load kernel: no requested CUDA kernel symbols were found in module.");
+}
+
+void AOTEngine::launch_paged(const KernelLaunchDescriptor& d, uintptr_t stream_ptr) {
+#if defined(KRT_MOCK_CUDA)
+  (void)d;
+  (void)stream_ptr;
+  throw std::runtime_error("Cannot launch the paged kernels: this is the host-only test build");
+#else
+  krt_qkv_paged_args a;
+  std::memset(&a, 0, sizeof(a));
+  a.x = reinterpret_cast<const void*>(d.input_ptr);
+  a.qkv_weight = reinterpret_cast<const void*>(d.qkv_weight_ptr);
+  a.qkv_bias = reinterpret_cast<const void*>(d.qkv_bias_ptr);
+  a.rms_weight = reinterpret_cast<const void*>(d.rms_weight_ptr);
+  a.rope_cos = reinterpret_cast<const float*>(d.freqs_cos_ptr);
+  a.rope_sin = reinterpret_cast<const float*>(d.freqs_sin_ptr);
+  a.positions = reinterpret_cast<const int32_t*>(d.positions_ptr);
+  a.token_seq = reinterpret_cast<const int32_t*>(d.token_seq_ptr);
+  a.block_table = reinterpret_cast<const int32_t*>(d.block_table_ptr);
+  a.kv_pool = reinterpret_cast<void*>(d.kv_pool_ptr);
+  a.q_out = reinterpret_cast<void*>(d.output_ptr);
+  a.k_out = reinterpret_cast<void*>(d.k_output_ptr);
+  a.v_out = reinterpret_cast<void*>(d.v_output_ptr);
+  a.num_tokens = d.seq_len;
+  a.d_model = d.d_model;
+  a.n_heads = d.n_heads;
+  a.n_kv_heads = d.n_kv_heads > 0 ? d.n_kv_heads : d.n_heads;
+  a.head_dim = d.head_dim;
+  a.x_stride = d.stride_x_seq > 0 ? d.stride_x_seq : d.d_model;
+  a.q_stride = d.stride_q_seq > 0 ? d.stride_q_seq : d.n_heads * d.head_dim;
+  a.max_position = d.max_position;
+  a.num_seqs = d.num_seqs;
+  a.block_table_stride = d.block_table_stride;
+  a.num_blocks = d.num_blocks;
+  a.tokens_per_block = d.tokens_per_block;
+  a.eps = d.eps;
+  a.workspace = reinterpret_cast<void*>(d.workspace_ptr);
+  a.workspace_bytes = d.workspace_bytes;
+  void* s = reinterpret_cast<void*>(stream_ptr);
+  const int rc = d.seq_len <= 256 ? krt_qkv_rope_decode(&a, s) : krt_qkv_rope_prefill(&a, s);
+  if (rc != KRT_OK) throw std::runtime_error(std::string("Cannot launch paged fused kernel: ") + krt_last_error());
+#endif
+}
+
+void AOTEngine::launch(const KernelLaunchDescriptor& d, uintptr_t stream_ptr) {
+  std::lock_guard<std::recursive_mutex> lock(mutex_);
+  if (d.kv_pool_ptr != 0) {
+    launch_paged(d, stream_ptr);
+    return;
+  }
+  if (!library_) throw std::runtime_error("Cannot launch AOT kernel: CUDA module is not loaded.");
+  if (d.input_ptr == 0 || d.output_ptr == 0)
+    throw std::runtime_error("Cannot launch AOT kernel: input and output buffers must be non-null.");
+  std::string name = d.kernel_name.empty() ? default_kernel_name_ : d.kernel_name;
+  if (d.kernel_name.empty() && name == "fused_rmsnorm_qkv_rope" && d.dtype == 3) name = "fused_rmsnorm_qkv_rope_bf16";
+  auto it = kernels_.find(name);
+  if (it == kernels_.end() || !it->second)
+    throw std::runtime_error("Cannot launch AOT kernel: selected CUDA function is not loaded: " + name);
+  if (d.block_x == 0 || d.block_y == 0 || d.block_z == 0 || d.grid_y == 0 || d.grid_z == 0)
+    throw std::runtime_error("Cannot launch AOT kernel: grid and block dimensions must be non-zero.");
+  unsigned grid_x = d.grid_x;
+  if (grid_x == 0) {
+    const long long work = d.seq_len > 0 ? d.seq_len : static_cast<long long>((d.byte_size + 3) / 4);
+    if (work <= 0)
+      throw std::runtime_error("Cannot launch AOT kernel: grid_x must be specified when seq_len and byte_size are empty.");
+    grid_x = static_cast<unsigned>((work + d.block_x - 1) / d.block_x);
+  }
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  void* in = reinterpret_cast<void*>(d.input_ptr);
+  void* out = reinterpret_cast<void*>(d.output_ptr);
+  int seq_len = d.seq_len;
+  size_t byte_size = d.byte_size;
+  if (name.rfind("fused_rmsnorm_qkv_rope", 0) == 0) {
+    if (!d.qkv_weight_ptr || !d.qkv_bias_ptr || !d.rms_weight_ptr || !d.freqs_cos_ptr || !d.freqs_sin_ptr ||
+        !d.k_output_ptr || !d.v_output_ptr)
+      throw std::runtime_error(
+          "Cannot launch fused_rmsnorm_qkv_rope: descriptor is missing required weight, frequency, or K/V output "
+          "buffers.");
+    if (d.seq_len <= 0 || d.d_model <= 0 || d.n_heads <= 0 || d.head_dim <= 0)
+      throw std::runtime_error(
+          "Cannot launch fused_rmsnorm_qkv_rope: seq_len, d_model, n_heads, and head_dim must be positive.");
+    if (d.block_x % 32 != 0 || d.block_y != 1 || d.block_z != 1 || d.block_x > 1024)
+      throw std::runtime_error("Cannot launch fused_rmsnorm_qkv_rope: block must be (32*k, 1, 1) with k <= 32.");
+    void* w = reinterpret_cast<void*>(d.qkv_weight_ptr);
+    void* b = reinterpret_cast<void*>(d.qkv_bias_ptr);
+    void* g = reinterpret_cast<void*>(d.rms_weight_ptr);
+    void* cs = reinterpret_cast<void*>(d.freqs_cos_ptr);
+    void* sn = reinterpret_cast<void*>(d.freqs_sin_ptr);
+    void* k = reinterpret_cast<void*>(d.k_output_ptr);
+    void* v = reinterpret_cast<void*>(d.v_output_ptr);
+    int d_model = d.d_model, n_heads = d.n_heads, head_dim = d.head_dim;
+    float eps = d.eps;
+    int s0 = d.stride_x_seq, s1 = d.stride_x_dim, s2 = d.stride_w_out, s3 = d.stride_w_in, s4 = d.stride_q_seq,
+        s5 = d.stride_q_dim, s6 = d.stride_k_seq, s7 = d.stride_k_dim, s8 = d.stride_v_seq, s9 = d.stride_v_dim;
+    void* params[] = {&in, &w, &b, &g, &cs, &sn, &out, &k, &v, &seq_len, &d_model, &n_heads, &head_dim, &eps,
+                      &s0, &s1, &s2, &s3, &s4, &s5, &s6, &s7, &s8, &s9};
+    // x_hat (d_model floats) + qkv (3 * n_heads * head_dim floats) + reduction scratch
+    size_t smem = (static_cast<size_t>(d_model) + 3 * static_cast<size_t>(n_heads) * head_dim + 32) * sizeof(float);
+    if (smem < d.shared_mem_bytes) smem = d.shared_mem_bytes;
+    if (smem > 48 * 1024)
+      KRT_CHECK_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(it->second),
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    KRT_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(it->second), dim3(grid_x, d.grid_y, d.grid_z),
+                                    dim3(d.block_x, d.block_y, d.block_z), params, smem, stream));
+    return;
+  }
+  void* params[] = {&in, &out, &seq_len, &byte_size};
+  KRT_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(it->second), dim3(grid_x, d.grid_y, d.grid_z),
+                                  dim3(d.block_x, d.block_y, d.block_z), params, d.shared_mem_bytes, stream));
+}
+
+void AOTEngine::launch(void* input_ptr, void* output_ptr, int seq_len, uintptr_t stream_ptr, size_t byte_size) {
+  KernelLaunchDescriptor d;
+  d.input_ptr = reinterpret_cast<uintptr_t>(input_ptr);
+  d.output_ptr = reinterpret_cast<uintptr_t>(output_ptr);
+  d.seq_len = seq_len;
+  d.byte_size = byte_size;
+  launch(d, stream_ptr);
+}
+
+void AOTEngine::launch_ptr(void* input_ptr, void* output_ptr, int seq_len, size_t byte_size) {
+  launch(input_ptr, output_ptr, seq_len, 0, byte_size);
+}
+
+void AOTEngine::synchronize_and_clear(uintptr_t stream_ptr) {
+  std::lock_guard<std::recursive_mutex> lock(mutex_);
+  KRT_CHECK_CUDA(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream_ptr)));
+}
