@@ -12,8 +12,9 @@ Inputs are synthetic (seeded N(0,1) activations, N(0, 0.02) weights,
 gamma = 1 + N(0, 0.1), block tables a seeded permutation of the pool).  Each
 step uses the weights of a different layer, cycling over enough layers that
 the weights touched between two uses of a layer exceed the 126 MB L2.
-Steps are CUDA-graph replays; the timed region is bracketed by a barrier and
-device synchronisation and timed with CUDA events, max over ranks.
+Steps are CUDA-graph replays (8 steps per graph, the kernels chained by
+programmatic dependent launch); the timed region is bracketed by a barrier
+and device synchronisation and timed with CUDA events, max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl krt|reference]
 
@@ -196,7 +197,10 @@ class Rig:
         if 2 in parts:
             self.lib.rowparallel_gemm_ar(self.comm_handle, da)
 
-    def graphs(self, parts=(0, 1, 2)):
+    def graphs(self, parts=(0, 1, 2), per_graph=1):
+        """One CUDA graph per starting layer; graph k holds steps
+        k*per_graph .. (k+1)*per_graph - 1, so replaying the graphs in order
+        walks the layers in order."""
         torch = self.torch
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -206,10 +210,11 @@ class Rig:
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         gs = []
-        for i in range(self.n_layers):
+        for k in range(self.n_layers):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self.step(i, parts)
+                for i in range(k * per_graph, (k + 1) * per_graph):
+                    self.step(i, parts)
             gs.append(g)
         return gs
 
@@ -237,12 +242,20 @@ def barrier(torch, world):
     torch.cuda.synchronize()
 
 
+STEPS_PER_GRAPH = 8
+
+
 def timed_graph_replays(torch, graphs, steps, world):
+    """Time exactly `steps` steps: graphs[0] holds STEPS_PER_GRAPH steps per
+    replay, graphs[1] one step (the remainder)."""
+    multi, single = graphs
     barrier(torch, world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(steps):
-        graphs[i % len(graphs)].replay()
+    for i in range(steps // STEPS_PER_GRAPH):
+        multi[i % len(multi)].replay()
+    for i in range(steps % STEPS_PER_GRAPH):
+        single[i % len(single)].replay()
     b.record()
     barrier(torch, world)
     return a.elapsed_time(b)  # ms
@@ -260,9 +273,9 @@ def run_krt(args, rank, world, local_rank):
         from python.kinetic_rt.dist import TPComm
         comm = TPComm(rank, world, max_n_out=HIDDEN)
     rig = Rig(torch, rank, world, comm)
-    graphs = rig.graphs()
+    graphs = (rig.graphs(per_graph=STEPS_PER_GRAPH), rig.graphs())
     for i in range(args.warmup):
-        graphs[i % len(graphs)].replay()
+        graphs[1][i % len(graphs[1])].replay()
     rig.check_status()
 
     clocks = ClockSampler(local_rank)
@@ -295,9 +308,9 @@ def run_krt(args, rank, world, local_rank):
         pass
     reps = max(min(args.steps, 2000), 2 * rig.n_layers)
     for part, (name, nbytes, what) in enumerate(kbytes):
-        g = rig.graphs(parts=(part,))
+        g = (rig.graphs(parts=(part,), per_graph=STEPS_PER_GRAPH), rig.graphs(parts=(part,)))
         for i in range(3):
-            g[i % len(g)].replay()
+            g[0][i % len(g[0])].replay()
         kms = max_over_ranks(torch, timed_graph_replays(torch, g, reps, world), world) / reps
         ach = nbytes / (kms * 1e-3) / 1e9
         kernels.append({"kernel": name, "bound": "hbm", "us": round(kms * 1e3, 3), "algorithmic_bytes": nbytes,

@@ -212,46 +212,54 @@ int env_int(const char* name, int dflt) {
   return (v && *v) ? std::atoi(v) : dflt;
 }
 
-int decode_stages(int n_pad, int kc) {
+int decode_stages(int n_pad, int kc, int splits) {
   for (int st = kMaxStages; st >= 1; --st)
-    if (decode_smem_bytes(st, n_pad, kc) <= 227 * 1024) return st;
+    if (decode_smem_bytes(st, n_pad, kc, splits) <= 227 * 1024) return st;
   return 0;
 }
 
 // 64-column chunks per decode pipeline stage (TMA box depth): the deepest of
 // 4, 2, 1 that divides the k-blocks and still leaves two pipeline stages.
 // KRT_DECODE_KC overrides the starting value for tuning.
-int decode_kc(int num_kb, int n_pad) {
+int decode_kc(int num_kb, int n_pad, int splits) {
   int kc = env_int("KRT_DECODE_KC", 4);
   if (kc < 1) kc = 1;
-  while (kc > 1 && ((num_kb % kc) != 0 || decode_stages(n_pad, kc) < 2)) kc >>= 1;
+  while (kc > 1 && ((num_kb % kc) != 0 || decode_stages(n_pad, kc, splits) < 2)) kc >>= 1;
   return kc;
 }
 
+struct DecodeCfg {
+  int kc, stages, splits;
+};
+
 // Split-K factor = cluster size along gridDim.y: as many splits as fit
 // (tiles * splits <= #SMs, at most 8 = portable cluster size) while every
-// cluster of the grid can be resident at once.  KRT_DECODE_SPLITS overrides.
-int decode_splits(int tiles, int num_kc, int n_pad, int stages, int kc) {
+// cluster of the grid can be resident at once; box depth and stage count
+// follow from the shared memory left beside the split's receive area.
+// KRT_DECODE_SPLITS overrides the split factor.
+DecodeCfg decode_config(int tiles, int num_kb, int n_pad) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, int, int>, int> cache;
+  static std::map<std::tuple<int, int, int, int>, DecodeCfg> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, tiles, num_kc, n_pad, stages, kc);
+  const auto key = std::make_tuple(dev, tiles, num_kb, n_pad);
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  int s = env_int("KRT_DECODE_SPLITS", 0);
-  if (s <= 0) {
-    s = device_sm_count() / tiles;
-    if (s > 8) s = 8;
-    if (s > num_kc) s = num_kc;
-    if (s < 1) s = 1;
-    while (s > 1 && decode_max_active_clusters(s, n_pad, stages, kc) < tiles) --s;
-  } else if (s > num_kc) {
-    s = num_kc;
+  DecodeCfg cfg{1, 1, 1};
+  const int forced = env_int("KRT_DECODE_SPLITS", 0);
+  int s = forced > 0 ? forced : device_sm_count() / tiles;
+  if (s > 8) s = 8;
+  if (s < 1) s = 1;
+  for (; s >= 1; --s) {
+    const int kc = decode_kc(num_kb, n_pad, s);
+    const int st = decode_stages(n_pad, kc, s);
+    if (st < 1 || s > num_kb / kc) continue;
+    cfg = DecodeCfg{kc, st, s};
+    if (forced > 0 || s == 1 || decode_max_active_clusters(s, n_pad, st, kc) >= tiles) break;
   }
-  cache[key] = s;
-  return s;
+  cache[key] = cfg;
+  return cfg;
 }
 
 }  // namespace
@@ -303,9 +311,10 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   p.num_blocks = a->num_blocks;
   p.tokens_per_block = a->tokens_per_block;
   p.eps = a->eps;
-  p.kc = decode_kc(num_kb, p.n_pad);
-  p.stages = decode_stages(p.n_pad, p.kc);
-  p.splits = decode_splits(tiles, num_kb / p.kc, p.n_pad, p.stages, p.kc);
+  const DecodeCfg cfg = decode_config(tiles, num_kb, p.n_pad);
+  p.kc = cfg.kc;
+  p.stages = cfg.stages;
+  p.splits = cfg.splits;
   int cols = 32;
   while (cols < p.n_pad) cols <<= 1;
   p.tmem_cols = cols;

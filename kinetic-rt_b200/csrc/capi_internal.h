@@ -27,7 +27,7 @@ cudaError_t launch_qkv_rope_generic(const GenericArgs& a, int dtype, int freqs_d
 size_t generic_smem_bytes(int d_model, int n_out);
 
 // qkv_decode.cu
-size_t decode_smem_bytes(int stages, int n_pad, int kc);
+size_t decode_smem_bytes(int stages, int n_pad, int kc, int splits);
 cudaError_t launch_qkv_rope_decode(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                    int tiles, cudaStream_t stream);
 
@@ -43,7 +43,7 @@ cudaError_t launch_qkv_rope_prefill(const CUtensorMap& tmap_w, const CUtensorMap
 
 // gemm_ar.cu
 struct GemmArParams;
-size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc);
+size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc, int splits);
 int gemm_ar_max_active_clusters(int splits, int n_pad, int stages, int kc);
 cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmArParams& p,
                                        int tiles, cudaStream_t stream);

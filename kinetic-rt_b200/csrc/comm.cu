@@ -16,6 +16,9 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <new>
 
 #include "../../include/krt.h"
@@ -272,18 +275,19 @@ extern "C" int krt_allreduce(krt_comm* c, const void* send, void* recv, size_t c
 // ------------------------------------------------------ fused GEMM + allreduce
 namespace {
 
-int gemm_stages(int n_pad, int kc) {
+int gemm_stages(int n_pad, int kc, int splits) {
   for (int st = kMaxStages; st >= 1; --st)
-    if (gemm_ar_smem_bytes(st, n_pad, kc) <= 227 * 1024) return st;
+    if (gemm_ar_smem_bytes(st, n_pad, kc, splits) <= 227 * 1024) return st;
   return 0;
 }
 
-int gemm_kc(int num_kb, int n_pad) {
+// Box depth with the most weight bytes in flight.
+int gemm_kc(int num_kb, int n_pad, int splits) {
   int best = 1;
   size_t best_bytes = 0;
   for (int kc = 4; kc >= 1; kc >>= 1) {
     if (num_kb % kc != 0) continue;
-    const size_t bytes = (size_t)gemm_stages(n_pad, kc) * kc * 16384;
+    const size_t bytes = (size_t)gemm_stages(n_pad, kc, splits) * kc * 16384;
     if (bytes > best_bytes) {
       best_bytes = bytes;
       best = kc;
@@ -292,13 +296,34 @@ int gemm_kc(int num_kb, int n_pad) {
   return best;
 }
 
-int gemm_splits(int tiles, int num_kc, int n_pad, int stages, int kc) {
+struct GemmCfg {
+  int kc, stages, splits;
+};
+
+// Split-K factor = cluster size: as many splits as fit (tiles * splits <=
+// #SMs, at most 8) while every cluster can be resident at once.
+GemmCfg gemm_config(int tiles, int num_kb, int n_pad) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, GemmCfg> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, tiles, num_kb, n_pad);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  GemmCfg cfg{1, 1, 1};
   int s = device_sm_count() / tiles;
   if (s > 8) s = 8;
-  if (s > num_kc) s = num_kc;
   if (s < 1) s = 1;
-  while (s > 1 && gemm_ar_max_active_clusters(s, n_pad, stages, kc) < tiles) --s;
-  return s;
+  for (; s >= 1; --s) {
+    const int kc = gemm_kc(num_kb, n_pad, s);
+    const int st = gemm_stages(n_pad, kc, s);
+    if (st < 1 || s > num_kb / kc) continue;
+    cfg = GemmCfg{kc, st, s};
+    if (s == 1 || gemm_ar_max_active_clusters(s, n_pad, st, kc) >= tiles) break;
+  }
+  cache[key] = cfg;
+  return cfg;
 }
 
 }  // namespace
@@ -343,9 +368,10 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
     p.num_tokens = T;
     p.n_pad = (T + 15) / 16 * 16;
-    p.kc = gemm_kc(num_kb, p.n_pad);
-    p.stages = gemm_stages(p.n_pad, p.kc);
-    p.splits = gemm_splits(tiles, num_kb / p.kc, p.n_pad, p.stages, p.kc);
+    const GemmCfg cfg = gemm_config(tiles, num_kb, p.n_pad);
+    p.kc = cfg.kc;
+    p.stages = cfg.stages;
+    p.splits = cfg.splits;
     int cols = 32;
     while (cols < p.n_pad) cols <<= 1;
     p.tmem_cols = cols;

@@ -14,7 +14,8 @@
 // 16*g8 .. +15) of chunk `ch` then owns 16 fp32 values of this rank's partial
 // product.
 //
-// Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1):
+// Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1;
+// every phase covers all the chunks a CTA finishes, one fence per CTA):
 //   1. reduce-scatter: the partial chunk (16 tokens x 128 features, fp32) is
 //      stored into the owner rank's staging slot [src][tile][chunk]
 //      (owner = tile % world) and a flag is released there;
@@ -43,17 +44,22 @@ struct GemmSmemTail {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t accum;
+  uint64_t recv;  // completes when the other ranks' partials of the owned chunks have arrived
   uint32_t tmem_base;
   int abort;
   int ok;
   int pad;
 };
 
-size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc) {
+// Pipeline buffers; after the main loop they hold the parked partial.
+__host__ __device__ inline size_t gemm_pipe_bytes(int stages, int n_pad, int kc) {
   size_t pipe = (size_t)stages * kc * (kGemmTileABytes + (size_t)n_pad * 128);
-  const size_t park = (size_t)n_pad * kYStride * sizeof(float);
-  if (pipe < park) pipe = park;
-  return 1024 + pipe + sizeof(GemmSmemTail);
+  if (pipe < park_area_bytes(n_pad)) pipe = park_area_bytes(n_pad);
+  return (pipe + 127) & ~size_t(127);
+}
+
+size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc, int splits) {
+  return 1024 + gemm_pipe_bytes(stages, n_pad, kc) + recv_area_bytes(n_pad, splits) + sizeof(GemmSmemTail);
 }
 
 __device__ __forceinline__ void gemm_fail(const GemmArParams& p, GemmSmemTail* tl, int code) {
@@ -87,9 +93,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t stage_bytes = a_stage + b_stage;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + (size_t)S * a_stage;
-  size_t pipe_bytes = (size_t)S * stage_bytes;
-  if (pipe_bytes < (size_t)n_pad * kYStride * sizeof(float)) pipe_bytes = (size_t)n_pad * kYStride * sizeof(float);
-  GemmSmemTail* tl = reinterpret_cast<GemmSmemTail*>(smem + pipe_bytes);
+  uint8_t* recv_smem = smem + gemm_pipe_bytes(S, n_pad, KC);
+  GemmSmemTail* tl = reinterpret_cast<GemmSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -105,8 +110,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tl->empty[s], 1);
     }
     mbar_init(&tl->accum, 1);
+    mbar_init(&tl->recv, 1);
     tl->abort = 0;
     fence_mbar_init();
+    // the partials this CTA will receive: (splits - 1) per owned chunk
+    mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
+                                         kChunkBytes);
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
@@ -117,6 +126,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  cluster_arrive_relaxed();  // the receive barriers are initialised; waited on before the first push
+  // The next kernel may launch onto free SMs now; it waits for this grid
+  // (griddepcontrol.wait) before touching anything this kernel writes.
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const uint32_t tmem_base = tl->tmem_base;
   volatile int* abort_flag = &tl->abort;
 
@@ -143,7 +156,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, row0, (kc0 + i) * KC, pol_w);
         tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (kc0 + i) * KC, pol_x);
       }
-      pdl_launch_dependents();  // the next kernel may start streaming its weights
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -168,163 +180,206 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       umma_commit(&tl->accum);
     }
   } else {
-    // park this CTA's partial accumulator, token-major
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16);
+    const int ept = threadIdx.x - 64;
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
     if (!waited && lane == 0) gemm_fail(p, tl, kStatusTimeoutAccum);
     tc_fence_after();
+    cluster_wait();
+
+    // Park the partial token-major in the idle pipeline buffers, one 16-token
+    // chunk at a time; a chunk finished by another cluster rank is sent to it
+    // by bulk copy as soon as it is parked.
+    const int crank = split;  // cluster (1, splits, 1): rank == blockIdx.y
+    const int nranks = p.splits;
     float* part = reinterpret_cast<float*>(smem);
-    if (waited) {
-      for (int c0 = 0; c0 < n_pad; c0 += 16) {
+    const uint32_t part_u32 = smem_u32(part);
+    for (int c = 0; c * 16 < n_pad; ++c) {
+      if (waited) {
         float v[16];
-        tmem_ld16(taddr + (uint32_t)c0, v);
+        tmem_ld16(taddr + (uint32_t)(c * 16), v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) part[(c0 + j) * kYStride + r] = v[j];
+        for (int jj = 0; jj < 16; ++jj) part[(c * 16 + jj) * kYStride + r] = v[jj];
+      }
+      const int cowner = c % nranks;
+      if (cowner != crank) {
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (ept == 0) {
+          const int slot = recv_slot(c / nranks, nranks, cowner, crank);
+          bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)cowner),
+                               part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
+                               map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)cowner));
+        }
       }
     }
-  }
+    if (ept == 0) bulk_commit_group();
+    named_bar_sync(1, 128);  // the owned chunks are parked
+    const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
+    if (!got && lane == 0) gemm_fail(p, tl, kStatusTimeoutCluster);
 
-  tc_fence_before();
-  cluster_sync();
-
-  if (warp >= 2) {
-    const int ept = threadIdx.x - 64;
+    // Thread (token j, features 16*g8 .. +15) of each chunk this CTA finishes
+    // (chunks crank, crank + splits, ...).  Each cross-GPU exchange phase
+    // covers all of the CTA's chunks at once, so a launch pays two NVLink
+    // round trips.
     const int j = ept >> 3, g8 = ept & 7;
-    const uint32_t crank = cluster_ctarank();
-    const uint32_t part_base = smem_u32(smem);
     const int T = p.num_tokens;
     const CommView& cv = p.comm;
     const int world = cv.world;
-    const int tiles = p.n_out / 128;
+    const bool alive = *abort_flag == 0;
+    const size_t slot_elems = (size_t)16 * 128;
+    const int owner = tile % world;
+    const float* recv = reinterpret_cast<const float*>(recv_smem);
     pdl_wait();  // Y and the exchange buffers may still be in use by the previous kernel
+    // ---- phase 1: this rank's partial of every chunk -> Y (one rank) or the owner's staging slot
     for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
       const int t = ch * 16 + j;
-      const bool live = t < T && *abort_flag == 0;
       float y[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) y[i] = 0.f;
-      for (int q = 0; q < p.splits; ++q) {
-        const uint32_t base = map_smem_to_rank(part_base, (uint32_t)q) + (uint32_t)(t * kYStride + 16 * g8) * 4u;
+      // partials of the cluster ranks, summed in rank order
+      const int oc = ch / nranks;
+      for (int q = 0; q < nranks; ++q) {
+        const float* src = q == crank ? part + t * kYStride + 16 * g8
+                                      : recv + (size_t)recv_slot(oc, nranks, crank, q) * (kChunkBytes / 4) +
+                                            (size_t)j * kYStride + 16 * g8;
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
-          const float4 a = ld_dsmem_f4(base + (uint32_t)k4 * 16u);
+          const float4 a = reinterpret_cast<const float4*>(src)[k4];
           y[4 * k4 + 0] += a.x;
           y[4 * k4 + 1] += a.y;
           y[4 * k4 + 2] += a.z;
           y[4 * k4 + 3] += a.w;
         }
       }
-      __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
       if (world == 1) {
-        if (live) {
+        if (alive && t < T) {
           uint4 a, b;
           pack16(y, a, b);
+          __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
           reinterpret_cast<uint4*>(ydst)[0] = a;
           reinterpret_cast<uint4*>(ydst)[1] = b;
         }
-        continue;
+      } else {
+        const size_t chunk_off = (((size_t)cv.rank * cv.L.tiles + tile) * kMaxChunks + ch) * slot_elems;
+        st_f4_x4(reinterpret_cast<float*>(cv.base[owner] + cv.L.staging_off) + chunk_off + j * 128 + 16 * g8, y);
       }
-      // -------- reduce-scatter: push the partial chunk to its owner
-      const int owner = tile % world;
-      const size_t slot_elems = (size_t)16 * 128;
-      const size_t chunk_off = (((size_t)cv.rank * cv.L.tiles + tile) * kMaxChunks + ch) * slot_elems;
-      float* stg = reinterpret_cast<float*>(cv.base[owner] + cv.L.staging_off) + chunk_off + j * 128 + 16 * g8;
-      st_f4_x4(stg, y);
-      __threadfence_system();
+    }
+    if (world > 1) {
       named_bar_sync(1, 128);
       if (ept == 0) {
+        fence_acq_rel_sys();
         uint32_t* pf = reinterpret_cast<uint32_t*>(cv.base[owner] + cv.L.part_flag_off);
-        st_release_sys(pf + ((size_t)tile * kMaxChunks + ch) * kMaxWorld + cv.rank, 1u);
+        for (int ch = (int)crank; ch * 16 < T; ch += p.splits)
+          st_release_sys(pf + ((size_t)tile * kMaxChunks + ch) * kMaxWorld + cv.rank, 1u);
       }
       if (cv.rank == owner) {
-        // -------- owner: reduce in rank order, broadcast bf16 results
+        // ---- phase 2 (owner): reduce every chunk in rank order, broadcast bf16 results
         if (ept == 0) {
-          uint32_t* pf = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.part_flag_off) +
-                         ((size_t)tile * kMaxChunks + ch) * kMaxWorld;
+          uint32_t* pf = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.part_flag_off);
           bool ok = true;
-          for (int q = 0; q < world && ok; ++q) ok = wait_flag_sys(pf + q, 1u);
-          if (ok)
-            for (int q = 0; q < world; ++q) pf[q] = 0u;
-          else
+          for (int ch = (int)crank; ch * 16 < T && ok; ch += p.splits)
+            for (int q = 0; q < world && ok; ++q) ok = wait_flag_sys(pf + ((size_t)tile * kMaxChunks + ch) * kMaxWorld + q, 1u);
+          if (ok) {
+            for (int ch = (int)crank; ch * 16 < T; ch += p.splits)
+              for (int q = 0; q < world; ++q) pf[((size_t)tile * kMaxChunks + ch) * kMaxWorld + q] = 0u;
+          } else {
             atomicOr(p.status, kStatusTimeoutPeer);
+          }
+          tl->ok = ok ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        const bool ok = tl->ok != 0;
+        if (ok) {
+          for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
+            const int t = ch * 16 + j;
+            float acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+            for (int q = 0; q < world; ++q) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  reinterpret_cast<const float*>(cv.base[cv.rank] + cv.L.staging_off) +
+                  (((size_t)q * cv.L.tiles + tile) * kMaxChunks + ch) * slot_elems + j * 128 + 16 * g8);
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4) {
+                const float4 a = __ldcg(src + k4);
+                acc[4 * k4 + 0] += a.x;
+                acc[4 * k4 + 1] += a.y;
+                acc[4 * k4 + 2] += a.z;
+                acc[4 * k4 + 3] += a.w;
+              }
+            }
+            if (t < T) {
+              uint4 a, b;
+              pack16(acc, a, b);
+              for (int q = 0; q < world; ++q) {
+                if (q == cv.rank) continue;
+                uint4* rd = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(cv.base[q] + cv.L.result_off) +
+                                                     (size_t)t * cv.L.max_n + row0 + 16 * g8);
+                rd[0] = a;
+                rd[1] = b;
+              }
+              __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
+              reinterpret_cast<uint4*>(ydst)[0] = a;
+              reinterpret_cast<uint4*>(ydst)[1] = b;
+            }
+          }
+        }
+        named_bar_sync(1, 128);
+        if (ept == 0 && ok) {
+          fence_acq_rel_sys();
+          for (int q = 0; q < world; ++q) {
+            if (q == cv.rank) continue;
+            uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[q] + cv.L.final_flag_off);
+            for (int ch = (int)crank; ch * 16 < T; ch += p.splits)
+              st_release_sys(ff + (size_t)tile * kMaxChunks + ch, 1u);
+          }
+        }
+      } else {
+        // ---- phase 3 (everyone else): wait for the owner's results, copy them into Y
+        if (ept == 0) {
+          uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.final_flag_off);
+          bool ok = true;
+          for (int ch = (int)crank; ch * 16 < T && ok; ch += p.splits) ok = wait_flag_sys(ff + (size_t)tile * kMaxChunks + ch, 1u);
+          if (ok) {
+            for (int ch = (int)crank; ch * 16 < T; ch += p.splits) ff[(size_t)tile * kMaxChunks + ch] = 0u;
+          } else {
+            atomicOr(p.status, kStatusTimeoutPeer);
+          }
           tl->ok = ok ? 1 : 0;
         }
         named_bar_sync(1, 128);
         if (tl->ok) {
-          float acc[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-          for (int q = 0; q < world; ++q) {
-            const float4* src = reinterpret_cast<const float4*>(
-                reinterpret_cast<const float*>(cv.base[cv.rank] + cv.L.staging_off) +
-                (((size_t)q * cv.L.tiles + tile) * kMaxChunks + ch) * slot_elems + j * 128 + 16 * g8);
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const float4 a = __ldcg(src + k4);
-              acc[4 * k4 + 0] += a.x;
-              acc[4 * k4 + 1] += a.y;
-              acc[4 * k4 + 2] += a.z;
-              acc[4 * k4 + 3] += a.w;
-            }
+          for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
+            const int t = ch * 16 + j;
+            if (t >= T) continue;
+            const uint4* rs = reinterpret_cast<const uint4*>(
+                reinterpret_cast<const __nv_bfloat16*>(cv.base[cv.rank] + cv.L.result_off) + (size_t)t * cv.L.max_n +
+                row0 + 16 * g8);
+            __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
+            reinterpret_cast<uint4*>(ydst)[0] = __ldcg(rs);
+            reinterpret_cast<uint4*>(ydst)[1] = __ldcg(rs + 1);
           }
-          uint4 a, b;
-          pack16(acc, a, b);
-          if (t < T) {
-            for (int q = 0; q < world; ++q) {
-              if (q == cv.rank) continue;
-              uint4* rd = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(cv.base[q] + cv.L.result_off) +
-                                                   (size_t)t * cv.L.max_n + row0 + 16 * g8);
-              rd[0] = a;
-              rd[1] = b;
-            }
-            reinterpret_cast<uint4*>(ydst)[0] = a;
-            reinterpret_cast<uint4*>(ydst)[1] = b;
-          }
-          __threadfence_system();
-        }
-        named_bar_sync(1, 128);
-        if (ept == 0 && tl->ok) {
-          for (int q = 0; q < world; ++q) {
-            if (q == cv.rank) continue;
-            uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[q] + cv.L.final_flag_off);
-            st_release_sys(ff + (size_t)tile * kMaxChunks + ch, 1u);
-          }
-        }
-      } else {
-        // -------- everyone else: wait for the owner's result, copy it into Y
-        if (ept == 0) {
-          uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.final_flag_off) +
-                         (size_t)tile * kMaxChunks + ch;
-          const bool ok = wait_flag_sys(ff, 1u);
-          if (ok)
-            *ff = 0u;
-          else
-            atomicOr(p.status, kStatusTimeoutPeer);
-          tl->ok = ok ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        if (tl->ok && t < T) {
-          const uint4* rs = reinterpret_cast<const uint4*>(
-              reinterpret_cast<const __nv_bfloat16*>(cv.base[cv.rank] + cv.L.result_off) + (size_t)t * cv.L.max_n +
-              row0 + 16 * g8);
-          reinterpret_cast<uint4*>(ydst)[0] = __ldcg(rs);
-          reinterpret_cast<uint4*>(ydst)[1] = __ldcg(rs + 1);
         }
       }
-      named_bar_sync(1, 128);  // tl->ok is reused by the next chunk
     }
-    (void)tiles;
+    if (ept == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }
 
-  cluster_sync();
-  if (warp == 1) tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+  if (warp < 2) cluster_wait();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+  }
 }
 
 cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmArParams& p,
                                        int tiles, cudaStream_t stream) {
-  const size_t smem = gemm_ar_smem_bytes(p.stages, p.n_pad, p.kc);
+  const size_t smem = gemm_ar_smem_bytes(p.stages, p.n_pad, p.kc, p.splits);
   cudaError_t e =
       cudaFuncSetAttribute(rowparallel_gemm_ar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -346,7 +401,7 @@ cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensor
 }
 
 int gemm_ar_max_active_clusters(int splits, int n_pad, int stages, int kc) {
-  const size_t smem = gemm_ar_smem_bytes(stages, n_pad, kc);
+  const size_t smem = gemm_ar_smem_bytes(stages, n_pad, kc, splits);
   if (cudaFuncSetAttribute(rowparallel_gemm_ar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return 0;

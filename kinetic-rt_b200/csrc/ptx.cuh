@@ -21,6 +21,7 @@ enum : int {
   kStatusBadBlock = 8,        // paged scatter: block id / position outside the pool
   kStatusTimeoutPeer = 16,    // cross-GPU flag wait ran out
   kStatusBadSplit = 32,       // split-K bookkeeping inconsistent
+  kStatusTimeoutCluster = 64, // partials from the other CTAs of the cluster did not arrive
 };
 
 // Wall-clock budget for any single wait: 2 s.
@@ -68,7 +69,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
+    if (abort && *abort) return false;
     if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
   }
 }
@@ -231,6 +232,17 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// Wait for data that other CTAs of the cluster send into this CTA's shared
+// memory.  The senders always send, also after their own failures, so this
+// wait ignores the CTA's abort flag (the CTA must not exit while copies may
+// still land) and allows two wait budgets, covering a sender that reaches
+// its send only after one of its own bounded waits ran out.
+__device__ __forceinline__ bool mbar_wait_warp_incoming(uint64_t* bar, uint32_t parity) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, nullptr) || mbar_wait(bar, parity, nullptr);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 // ----------------------------------------------------------------- cluster
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -242,18 +254,41 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
+// Split cluster barrier: arrive early (after the mbarrier inits), wait
+// later, right before the first access to another CTA's shared memory.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// Bulk copy of `bytes` (multiple of 16, 16-byte aligned ends) from this
+// CTA's shared memory to shared memory of another CTA of the cluster; the
+// transfer completes `bytes` of transaction count on the mbarrier at
+// `mbar_cluster` (an address in the destination CTA).
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src_smem, uint32_t bytes,
+                                                     uint32_t mbar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(src_smem), "r"(bytes), "r"(mbar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the source buffers of all committed bulk copies have been read.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 // Address of the same shared-memory location in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_smem_to_rank(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
 }
+// No memory clobber: the loads stay ordered after the (volatile) cluster
+// barrier but may be issued back to back, so their latencies overlap.
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
-               : "memory");
+               : "r"(cluster_addr));
   return v;
 }
 
@@ -269,6 +304,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Orders this thread's earlier memory operations, and those of threads that
+// synchronised with it through a barrier, before its later ones, system-wide.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 // Wait until *flag == expect; false after kWaitBudgetNs.
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t expect) {
   if (ld_acquire_sys(flag) == expect) return true;

@@ -43,12 +43,29 @@ struct DecodeSmemTail {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t accum;
+  uint64_t recv;  // completes when the other ranks' partials of the owned chunks have arrived
   uint32_t tmem_base;
   int abort;
-  int pad[2];
   int pos[256];
   long long slot[256];
 };
+
+// Pipeline buffers; after the main loop they hold the parked partial.
+__host__ __device__ inline size_t decode_pipe_bytes(int stages, int n_pad, int kc) {
+  size_t pipe = (size_t)stages * kc * (kTileABytes + (size_t)n_pad * 128);
+  if (pipe < park_area_bytes(n_pad)) pipe = park_area_bytes(n_pad);
+  return (pipe + 127) & ~size_t(127);
+}
+
+__device__ __forceinline__ void add_f4x4(float* y, const float4* a) {
+#pragma unroll
+  for (int k4 = 0; k4 < 4; ++k4) {
+    y[4 * k4 + 0] += a[k4].x;
+    y[4 * k4 + 1] += a[k4].y;
+    y[4 * k4 + 2] += a[k4].z;
+    y[4 * k4 + 3] += a[k4].w;
+  }
+}
 
 __device__ __forceinline__ void decode_fail(const PagedParams& p, DecodeSmemTail* tl, int code) {
   atomicOr(p.status, code);
@@ -69,9 +86,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   const uint32_t stage_bytes = a_stage + b_stage;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + (size_t)S * a_stage;
-  size_t pipe_bytes = (size_t)S * stage_bytes;
-  if (pipe_bytes < (size_t)n_pad * kYStride * sizeof(float)) pipe_bytes = (size_t)n_pad * kYStride * sizeof(float);
-  DecodeSmemTail* tl = reinterpret_cast<DecodeSmemTail*>(smem + pipe_bytes);
+  const size_t pipe_bytes = decode_pipe_bytes(S, n_pad, KC);
+  uint8_t* recv_smem = smem + pipe_bytes;
+  DecodeSmemTail* tl = reinterpret_cast<DecodeSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -87,8 +104,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       mbar_init(&tl->empty[s], 1);
     }
     mbar_init(&tl->accum, 1);
+    mbar_init(&tl->recv, 1);
     tl->abort = 0;
     fence_mbar_init();
+    // the partials this CTA will receive: (splits - 1) per owned chunk
+    mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
+                                         kChunkBytes);
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
@@ -99,8 +120,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  cluster_arrive_relaxed();  // the receive barriers are initialised; waited on before the first push
+  // The next kernel may launch onto free SMs now; it waits for this grid
+  // (griddepcontrol.wait) before touching anything this kernel writes.
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const uint32_t tmem_base = tl->tmem_base;
   volatile int* abort_flag = &tl->abort;
+  // Epilogue warps: RoPE values of the first finished token and the bias of
+  // the thread's row groups, fetched before the main loop ends.
+  float4 cs0[4], sn0[4];
+  float bias_y[16], bias_p[16];
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -164,93 +193,120 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       tl->pos[t] = p.tok_pos[t];
       tl->slot[t] = p.tok_slot[t];
     }
+    {
+      // RoPE values of this thread's first phase-B token, fetched while the
+      // main loop runs (same (token, row group) mapping as phase B).
+      const int t0 = (int)cluster_ctarank() * 16 + (ept >> 3);
+      if (t0 < T && tile < p.n_heads + p.n_kv_heads) load_rope16(p, p.tok_pos[t0], ept & 7, cs0, sn0);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        bias_y[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * (ept & 7) + i]) : 0.f;
+        bias_p[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * ((ept & 7) ^ 4) + i]) : 0.f;
+      }
+    }
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
     if (!waited && lane == 0) decode_fail(p, tl, kStatusTimeoutAccum);
     tc_fence_after();
-    float* part = reinterpret_cast<float*>(smem);  // pipeline buffers are idle now
-    if (waited) {
-      for (int c0 = 0; c0 < n_pad; c0 += 16) {
+    cluster_wait();
+
+    // Park the partial token-major in the idle pipeline buffers, one 16-token
+    // chunk at a time; a chunk finished by another rank is sent to it by bulk
+    // copy as soon as it is parked.
+    const int rank = split;  // cluster (1, splits, 1): rank == blockIdx.y
+    const int nranks = p.splits;
+    float* part = reinterpret_cast<float*>(smem);
+    const uint32_t part_u32 = smem_u32(part);
+    for (int c = 0; c * 16 < n_pad; ++c) {
+      if (waited) {
         float v[16];
-        tmem_ld16(taddr + (uint32_t)c0, v);
+        tmem_ld16(taddr + (uint32_t)(c * 16), v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) part[(c0 + j) * kYStride + r] = v[j];
+        for (int jj = 0; jj < 16; ++jj) part[(c * 16 + jj) * kYStride + r] = v[jj];
+      }
+      const int owner = c % nranks;
+      if (owner != rank) {
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (ept == 0) {
+          const int slot = recv_slot(c / nranks, nranks, owner, rank);
+          bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)owner),
+                               part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
+                               map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)owner));
+        }
       }
     }
-  }
+    if (ept == 0) bulk_commit_group();
+    named_bar_sync(1, 128);  // the owned chunks are parked
 
-  tc_fence_before();
-  cluster_sync();  // every partial of the cluster is parked
-
-  if (warp >= 2) {
-    // ------------------------------------------------ epilogue, phase B
-    // CTA `rank` finalises chunks rank, rank + splits, ...; thread (j, g8)
-    // owns token c*16 + j and rows 16*g8 .. +15.
-    const int ept = threadIdx.x - 64;
+    // ------------------------------------------------ finish the owned chunks
+    // thread (j, g8) owns token c*16 + j and rows 16*g8 .. +15 of chunk c.
     const int j = ept >> 3, g8 = ept & 7;
-    const uint32_t rank = cluster_ctarank();
-    const int nranks = p.splits;
-    const uint32_t part_base = smem_u32(smem);
     const bool rot = tile < p.n_heads + p.n_kv_heads;
     const int gp = g8 ^ 4;
-    float bias_y[16], bias_p[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      bias_y[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * g8 + i]) : 0.f;
-      bias_p[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * gp + i]) : 0.f;
-    }
-    if (*abort_flag == 0) {
-      for (int c = (int)rank; c * 16 < p.num_tokens; c += nranks) {
+    const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
+    if (!got && lane == 0) decode_fail(p, tl, kStatusTimeoutCluster);
+    if (got && *abort_flag == 0) {
+      const float* recv = reinterpret_cast<const float*>(recv_smem);
+      for (int c = rank; c * 16 < T; c += nranks) {
         const int t = c * 16 + j;
-        if (t >= p.num_tokens) continue;
+        if (t >= T) continue;
         const int pos = tl->pos[t];
         float4 cs[4], sn[4];
-        if (rot) load_rope16(p, pos, g8, cs, sn);
+        if (rot) {
+          if (c == rank) {
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              cs[k4] = cs0[k4];
+              sn[k4] = sn0[k4];
+            }
+          } else {
+            load_rope16(p, pos, g8, cs, sn);
+          }
+        }
         float y[16], yp[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           y[i] = bias_y[i];
           yp[i] = bias_p[i];
         }
+        // partials summed in rank order
+        const int oc = c / nranks;
         for (int q = 0; q < nranks; ++q) {
-          const uint32_t base = map_smem_to_rank(part_base, (uint32_t)q) + (uint32_t)(t * kYStride) * 4u;
+          const float* src = q == rank ? part + t * kYStride
+                                       : recv + (size_t)recv_slot(oc, nranks, rank, q) * (kChunkBytes / 4) +
+                                             (size_t)j * kYStride;
+          float4 a[4], b[4];
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const float4 a = ld_dsmem_f4(base + (uint32_t)(16 * g8 + 4 * k4) * 4u);
-            y[4 * k4 + 0] += a.x;
-            y[4 * k4 + 1] += a.y;
-            y[4 * k4 + 2] += a.z;
-            y[4 * k4 + 3] += a.w;
-          }
+          for (int k4 = 0; k4 < 4; ++k4) a[k4] = reinterpret_cast<const float4*>(src + 16 * g8)[k4];
           if (rot) {
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const float4 a = ld_dsmem_f4(base + (uint32_t)(16 * gp + 4 * k4) * 4u);
-              yp[4 * k4 + 0] += a.x;
-              yp[4 * k4 + 1] += a.y;
-              yp[4 * k4 + 2] += a.z;
-              yp[4 * k4 + 3] += a.w;
-            }
+            for (int k4 = 0; k4 < 4; ++k4) b[k4] = reinterpret_cast<const float4*>(src + 16 * gp)[k4];
           }
+          add_f4x4(y, a);
+          if (rot) add_f4x4(yp, b);
         }
         store_rows16(p, tile, t, g8, pos, tl->slot[t], y, yp, cs, sn);
       }
     }
+    if (ept == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }
 
-  cluster_sync();  // no CTA leaves while others still read its partial
-  if (warp == 1) tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+  if (warp < 2) cluster_wait();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+  }
 }
 
-size_t decode_smem_bytes(int stages, int n_pad, int kc) {
-  size_t pipe = (size_t)stages * kc * (kTileABytes + (size_t)n_pad * 128);
-  const size_t park = (size_t)n_pad * kYStride * sizeof(float);
-  if (pipe < park) pipe = park;
-  return 1024 + pipe + sizeof(DecodeSmemTail);
+size_t decode_smem_bytes(int stages, int n_pad, int kc, int splits) {
+  return 1024 + decode_pipe_bytes(stages, n_pad, kc) + recv_area_bytes(n_pad, splits) + sizeof(DecodeSmemTail);
 }
 
 cudaError_t launch_qkv_rope_decode(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                    int tiles, cudaStream_t stream) {
-  const size_t smem = decode_smem_bytes(p.stages, p.n_pad, p.kc);
+  const size_t smem = decode_smem_bytes(p.stages, p.n_pad, p.kc, p.splits);
   cudaError_t e = cudaFuncSetAttribute(qkv_rope_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -272,7 +328,7 @@ cudaError_t launch_qkv_rope_decode(const CUtensorMap& tmap_w, const CUtensorMap&
 
 // Largest cluster count that can be resident at once for a given split.
 int decode_max_active_clusters(int splits, int n_pad, int stages, int kc) {
-  const size_t smem = decode_smem_bytes(stages, n_pad, kc);
+  const size_t smem = decode_smem_bytes(stages, n_pad, kc, splits);
   if (cudaFuncSetAttribute(qkv_rope_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return 0;

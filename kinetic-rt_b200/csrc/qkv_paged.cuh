@@ -156,6 +156,24 @@ __device__ __forceinline__ void store_rows16(const PagedParams& p, int tile, int
 // Row stride (floats) of the token-major staging buffers: 128 rows + 4 pad.
 constexpr int kYStride = 132;
 
+// Split-K exchange inside a cluster.  Each CTA parks its fp32 partial tile
+// token-major ([n_pad][kYStride]); the 16-token chunk c is finished by
+// cluster rank c % splits, which receives the other ranks' partials of that
+// chunk by bulk copy into its receive area:
+//   slot(oc, q) = oc * (splits - 1) + (q < owner ? q : q - 1)
+// for its oc-th owned chunk and source rank q.
+constexpr uint32_t kChunkBytes = 16u * kYStride * 4u;  // one chunk of a partial
+__host__ __device__ inline int owned_chunks(int n_chunks, int splits, int rank) {
+  return rank < n_chunks ? (n_chunks - 1 - rank) / splits + 1 : 0;
+}
+__host__ __device__ inline size_t recv_area_bytes(int n_pad, int splits) {
+  return splits > 1 ? (size_t)owned_chunks(n_pad / 16, splits, 0) * (splits - 1) * kChunkBytes : 0;
+}
+__host__ __device__ inline size_t park_area_bytes(int n_pad) { return (size_t)n_pad * kYStride * sizeof(float); }
+__host__ __device__ inline int recv_slot(int oc, int splits, int owner, int q) {
+  return oc * (splits - 1) + (q < owner ? q : q - 1);
+}
+
 __device__ __forceinline__ void ld_smem_16f(const float* src, float* dst) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
