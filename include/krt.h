@@ -172,7 +172,11 @@ KRT_API int krt_qkv_rope_decode_noalloc(const krt_qkv_paged_args* args, void* st
 
 /* Copy the device status word of a workspace to the host (synchronises the
  * stream), clear it, and return KRT_OK or KRT_ERR_DEVICE with the bits in
- * *bits. */
+ * *bits.  Bits: 1 / 2 / 4 pipeline waits of a kernel ran out (full stage,
+ * free stage, accumulator), 8 a token's position or pool block lies outside
+ * the table or pool, 16 a wait for another GPU ran out, 32 inconsistent
+ * split-K bookkeeping, 64 partials from the other CTAs of a thread-block
+ * cluster did not arrive. */
 KRT_API int krt_read_status(void* workspace, void* stream, int32_t* bits);
 
 /* -------------------------------------------------------------------------

@@ -17,6 +17,7 @@ constexpr int kMaxWorld = 8;
 constexpr int kArMaxCtas = 64;     // CTAs of the standalone allreduce
 constexpr int kChunkTokens = 16;   // token granularity of the fused exchange
 constexpr int kMaxChunks = 16;     // 256 tokens per launch
+constexpr int kMaxEpochCtas = 4096;  // CTAs of one fused launch with a launch counter
 
 struct CommLayout {
   int world, max_n, tiles;
@@ -26,6 +27,17 @@ struct CommLayout {
   size_t final_flag_off;   // u32 [tiles][kMaxChunks]
   size_t ar_part_off;      // u32 [kArMaxCtas][kMaxWorld]
   size_t ar_final_off;     // u32 [kMaxWorld][kArMaxCtas]
+  // Fused GEMM + allreduce exchange in flagged words: every 8-byte word is
+  // (launch epoch << 32) | 32 payload bits, written with one 8-byte store,
+  // so a reader that sees the current epoch in a word also sees its payload
+  // and no fence or separate flag is needed.
+  // Both areas hold per-chunk slots laid out [word pair][finishing thread]
+  // (16 bytes per thread and pair), so a warp's store covers 512
+  // contiguous bytes.
+  size_t ll_stage_off;     // [world (source)][owned tiles][kMaxChunks][8 pairs][128 threads] fp32 payload
+  size_t ll_result_off;    // [tiles][kMaxChunks][4 pairs][128 threads]                       bf16x2 payload
+  size_t epoch_off;        // u32 [kMaxEpochCtas] launches seen by each CTA index
+  int owned_tiles;         // ceil(tiles / world): tile t is reduced by rank t % world
   size_t total;
 };
 
@@ -41,7 +53,11 @@ inline CommLayout comm_layout(int world, int max_n) {
   L.final_flag_off = up(L.part_flag_off + (size_t)L.tiles * kMaxChunks * kMaxWorld * 4);
   L.ar_part_off = up(L.final_flag_off + (size_t)L.tiles * kMaxChunks * 4);
   L.ar_final_off = up(L.ar_part_off + (size_t)kArMaxCtas * kMaxWorld * 4);
-  L.total = up(L.ar_final_off + (size_t)kMaxWorld * kArMaxCtas * 4);
+  L.owned_tiles = (L.tiles + world - 1) / world;
+  L.ll_stage_off = up(L.ar_final_off + (size_t)kMaxWorld * kArMaxCtas * 4);
+  L.ll_result_off = up(L.ll_stage_off + (size_t)world * L.owned_tiles * kMaxChunks * 16 * 128 * 8);
+  L.epoch_off = up(L.ll_result_off + (size_t)L.tiles * kMaxChunks * 4 * 128 * 16);
+  L.total = up(L.epoch_off + (size_t)kMaxEpochCtas * 4);
   return L;
 }
 

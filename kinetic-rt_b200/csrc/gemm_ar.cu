@@ -9,24 +9,29 @@
 //
 // GEMM part (same structure as the decode QKV kernel): swap-AB, UMMA M = 128
 // output features per tile, N = padded tokens, W and X tiles by TMA in
-// {64, rows, KC} boxes, split-K across a thread-block cluster with the
-// partial tiles reduced over DSMEM.  The finishing thread (token j, features
-// 16*g8 .. +15) of chunk `ch` then owns 16 fp32 values of this rank's partial
-// product.
+// {64, rows, KC} boxes, split-K across a thread-block cluster whose ranks
+// send each other their partial chunks by bulk DSMEM copy.  The finishing
+// thread (token j, features 16*g8 .. +15) of chunk `ch` then owns 16 fp32
+// values of this rank's partial product.
 //
-// Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1;
-// every phase covers all the chunks a CTA finishes, one fence per CTA):
+// Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1),
+// in flagged 8-byte words ((launch epoch << 32) | payload, one store each),
+// so that no memory fence and no separate flag is on the path:
 //   1. reduce-scatter: the partial chunk (16 tokens x 128 features, fp32) is
-//      stored into the owner rank's staging slot [src][tile][chunk]
-//      (owner = tile % world) and a flag is released there;
-//   2. the owner's CTA for the same chunk waits for all `world` flags, sums
-//      the partials in rank order (so every rank ends with bit-identical
-//      values), writes bf16 results into every rank's result buffer and its
-//      own Y, then releases a flag on each peer;
-//   3. every other rank's CTA for that chunk waits for that flag and copies
-//      the chunk from its result buffer into Y.
-// Flags are reset by their consumer, so the protocol needs no epoch and can
-// be replayed from a CUDA graph.  All waits are bounded (status bit 16).
+//      stored into the owner rank's stage [src][tile / world][chunk]
+//      (owner = tile % world);
+//   2. the owner's CTA for the same chunk polls the words of all `world`
+//      ranks, sums the partials in rank order (so every rank ends with
+//      bit-identical values), writes the bf16 result to its own Y and, as
+//      flagged bf16x2 words, into every peer's result area;
+//   3. every other rank's CTA for that chunk polls those words and copies
+//      them into Y.
+// The epoch of a launch is a per-CTA-index launch counter kept in the
+// communicator's own buffer, identical on all ranks because all ranks run
+// the same launches; stale words of an earlier launch never match, so the
+// protocol needs no reset and replays from a CUDA graph.  A slot is only
+// rewritten by a launch that the reader's progress already allowed.  All
+// polls are bounded (status bit 16).
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -47,7 +52,7 @@ struct GemmSmemTail {
   uint64_t recv;  // completes when the other ranks' partials of the owned chunks have arrived
   uint32_t tmem_base;
   int abort;
-  int ok;
+  uint32_t epoch;
   int pad;
 };
 
@@ -67,10 +72,16 @@ __device__ __forceinline__ void gemm_fail(const GemmArParams& p, GemmSmemTail* t
   tl->abort = 1;
 }
 
-__device__ __forceinline__ void st_f4_x4(float* dst, const float* v) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+// Flagged-word areas of the fused exchange (see CommLayout).
+// Slot of one chunk; the word pair i of finishing thread `ept` is at
+// slot + 2 * (i * 128 + ept).
+__device__ __forceinline__ uint64_t* ll_stage(const CommView& cv, int holder, int src, int tile, int ch) {
+  return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_stage_off) +
+         (((size_t)src * cv.L.owned_tiles + tile / cv.world) * kMaxChunks + ch) * (8 * 128 * 2);
+}
+__device__ __forceinline__ uint64_t* ll_result(const CommView& cv, int holder, int tile, int ch) {
+  return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_result_off) +
+         ((size_t)tile * kMaxChunks + ch) * (4 * 128 * 2);
 }
 
 __device__ __forceinline__ void pack16(const float* v, uint4& a, uint4& b) {
@@ -189,29 +200,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     cluster_wait();
 
-    // Park the partial token-major in the idle pipeline buffers, one 16-token
-    // chunk at a time; a chunk finished by another cluster rank is sent to it
-    // by bulk copy as soon as it is parked.
+    // Park the partial token-major in the idle pipeline buffers, four 16-token
+    // chunks at a time; a chunk finished by another cluster rank is sent to it
+    // by bulk copy as soon as its group is parked.
     const int crank = split;  // cluster (1, splits, 1): rank == blockIdx.y
     const int nranks = p.splits;
     float* part = reinterpret_cast<float*>(smem);
     const uint32_t part_u32 = smem_u32(part);
-    for (int c = 0; c * 16 < n_pad; ++c) {
+    const int n_chunks = n_pad / 16;
+    for (int c0 = 0; c0 < n_chunks; c0 += 4) {
+      const int nc = n_chunks - c0 < 4 ? n_chunks - c0 : 4;
       if (waited) {
-        float v[16];
-        tmem_ld16(taddr + (uint32_t)(c * 16), v);
+        uint32_t v[4][16];
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) part[(c * 16 + jj) * kYStride + r] = v[jj];
+        for (int cc = 0; cc < 4; ++cc)
+          if (cc < nc) tmem_ld16_nowait(taddr + (uint32_t)((c0 + cc) * 16), v[cc]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          if (cc < nc) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * kYStride + r] = __uint_as_float(v[cc][jj]);
+          }
       }
-      const int cowner = c % nranks;
-      if (cowner != crank) {
+      bool remote = false;
+      for (int cc = 0; cc < nc; ++cc) remote |= (c0 + cc) % nranks != crank;
+      if (remote) {
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (ept == 0) {
-          const int slot = recv_slot(c / nranks, nranks, cowner, crank);
-          bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)cowner),
-                               part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
-                               map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)cowner));
+          for (int cc = 0; cc < nc; ++cc) {
+            const int c = c0 + cc, cowner = c % nranks;
+            if (cowner == crank) continue;
+            const int slot = recv_slot(c / nranks, nranks, cowner, crank);
+            bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)cowner),
+                                 part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
+                                 map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)cowner));
+          }
         }
       }
     }
@@ -224,34 +249,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // (chunks crank, crank + splits, ...).  Each cross-GPU exchange phase
     // covers all of the CTA's chunks at once, so a launch pays two NVLink
     // round trips.
-    const int j = ept >> 3, g8 = ept & 7;
+    const int j = ept & 15, g8 = ept >> 4;  // 8 consecutive lanes: 8 tokens, one row group (no bank conflicts)
     const int T = p.num_tokens;
     const CommView& cv = p.comm;
     const int world = cv.world;
     const bool alive = *abort_flag == 0;
-    const size_t slot_elems = (size_t)16 * 128;
     const int owner = tile % world;
     const float* recv = reinterpret_cast<const float*>(recv_smem);
     pdl_wait();  // Y and the exchange buffers may still be in use by the previous kernel
+    // Launch epoch of this CTA index: the same on every rank, since every
+    // rank runs the same launches; it tags this launch's flagged words.
+    uint32_t epoch = 0;
+    if (world > 1) {
+      if (ept == 0) {
+        uint32_t* ctr =
+            reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.epoch_off) + (blockIdx.y * gridDim.x + blockIdx.x);
+        const uint32_t e = __ldcg(ctr) + 1u;
+        *ctr = e;
+        tl->epoch = e;
+      }
+      named_bar_sync(1, 128);
+      epoch = tl->epoch;
+    }
     // ---- phase 1: this rank's partial of every chunk -> Y (one rank) or the owner's staging slot
     for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
       const int t = ch * 16 + j;
       float y[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) y[i] = 0.f;
-      // partials of the cluster ranks, summed in rank order
+      // partials of the cluster ranks, summed in rank order; four ranks per
+      // round with all their loads issued before the first add
       const int oc = ch / nranks;
-      for (int q = 0; q < nranks; ++q) {
-        const float* src = q == crank ? part + t * kYStride + 16 * g8
-                                      : recv + (size_t)recv_slot(oc, nranks, crank, q) * (kChunkBytes / 4) +
-                                            (size_t)j * kYStride + 16 * g8;
+      for (int q0 = 0; q0 < nranks; q0 += 4) {
+        float4 a[4][4];
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const float4 a = reinterpret_cast<const float4*>(src)[k4];
-          y[4 * k4 + 0] += a.x;
-          y[4 * k4 + 1] += a.y;
-          y[4 * k4 + 2] += a.z;
-          y[4 * k4 + 3] += a.w;
+        for (int qq = 0; qq < 4; ++qq) {
+          const int q = q0 + qq < nranks ? q0 + qq : q0;
+          const float* src = q == crank ? part + t * kYStride + 16 * g8
+                                        : recv + (size_t)recv_slot(oc, nranks, crank, q) * (kChunkBytes / 4) +
+                                              (size_t)j * kYStride + 16 * g8;
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) a[qq][k4] = reinterpret_cast<const float4*>(src)[k4];
+        }
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          if (q0 + qq >= nranks) break;
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            y[4 * k4 + 0] += a[qq][k4].x;
+            y[4 * k4 + 1] += a[qq][k4].y;
+            y[4 * k4 + 2] += a[qq][k4].z;
+            y[4 * k4 + 3] += a[qq][k4].w;
+          }
         }
       }
       if (world == 1) {
@@ -263,107 +312,68 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           reinterpret_cast<uint4*>(ydst)[1] = b;
         }
       } else {
-        const size_t chunk_off = (((size_t)cv.rank * cv.L.tiles + tile) * kMaxChunks + ch) * slot_elems;
-        st_f4_x4(reinterpret_cast<float*>(cv.base[owner] + cv.L.staging_off) + chunk_off + j * 128 + 16 * g8, y);
+        // one flagged fp32 word per value into the owner's stage (local when this rank owns the tile)
+        uint64_t* dst = ll_stage(cv, owner, cv.rank, tile, ch) + 2 * ept;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          st_ll2(dst + 256 * i, ll_word(__float_as_uint(y[2 * i]), epoch),
+                 ll_word(__float_as_uint(y[2 * i + 1]), epoch));
       }
     }
     if (world > 1) {
-      named_bar_sync(1, 128);
-      if (ept == 0) {
-        fence_acq_rel_sys();
-        uint32_t* pf = reinterpret_cast<uint32_t*>(cv.base[owner] + cv.L.part_flag_off);
-        for (int ch = (int)crank; ch * 16 < T; ch += p.splits)
-          st_release_sys(pf + ((size_t)tile * kMaxChunks + ch) * kMaxWorld + cv.rank, 1u);
-      }
+      const uint64_t t0 = globaltimer_ns();
+      bool ok = true;
       if (cv.rank == owner) {
-        // ---- phase 2 (owner): reduce every chunk in rank order, broadcast bf16 results
-        if (ept == 0) {
-          uint32_t* pf = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.part_flag_off);
-          bool ok = true;
-          for (int ch = (int)crank; ch * 16 < T && ok; ch += p.splits)
-            for (int q = 0; q < world && ok; ++q) ok = wait_flag_sys(pf + ((size_t)tile * kMaxChunks + ch) * kMaxWorld + q, 1u);
-          if (ok) {
-            for (int ch = (int)crank; ch * 16 < T; ch += p.splits)
-              for (int q = 0; q < world; ++q) pf[((size_t)tile * kMaxChunks + ch) * kMaxWorld + q] = 0u;
-          } else {
-            atomicOr(p.status, kStatusTimeoutPeer);
-          }
-          tl->ok = ok ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        const bool ok = tl->ok != 0;
-        if (ok) {
-          for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
-            const int t = ch * 16 + j;
-            float acc[16];
+        // ---- phase 2 (owner): every rank's words of the chunk, reduced in rank
+        // order; the bf16 result goes to Y and, as flagged words, to every peer
+        for (int ch = crank; ch * 16 < T; ch += p.splits) {
+          const int t = ch * 16 + j;
+          float acc[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-            for (int q = 0; q < world; ++q) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  reinterpret_cast<const float*>(cv.base[cv.rank] + cv.L.staging_off) +
-                  (((size_t)q * cv.L.tiles + tile) * kMaxChunks + ch) * slot_elems + j * 128 + 16 * g8);
+          for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+          for (int q = 0; q < world; ++q) {
+            const uint64_t* src = ll_stage(cv, cv.rank, q, tile, ch) + 2 * ept;
 #pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4) {
-                const float4 a = __ldcg(src + k4);
-                acc[4 * k4 + 0] += a.x;
-                acc[4 * k4 + 1] += a.y;
-                acc[4 * k4 + 2] += a.z;
-                acc[4 * k4 + 3] += a.w;
-              }
-            }
-            if (t < T) {
-              uint4 a, b;
-              pack16(acc, a, b);
-              for (int q = 0; q < world; ++q) {
-                if (q == cv.rank) continue;
-                uint4* rd = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(cv.base[q] + cv.L.result_off) +
-                                                     (size_t)t * cv.L.max_n + row0 + 16 * g8);
-                rd[0] = a;
-                rd[1] = b;
-              }
-              __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
-              reinterpret_cast<uint4*>(ydst)[0] = a;
-              reinterpret_cast<uint4*>(ydst)[1] = b;
+            for (int i = 0; i < 8; ++i) {
+              uint32_t u0 = 0, u1 = 0;
+              if (ok) ok = poll_ll2(src + 256 * i, epoch, t0, u0, u1);
+              acc[2 * i] += __uint_as_float(u0);
+              acc[2 * i + 1] += __uint_as_float(u1);
             }
           }
-        }
-        named_bar_sync(1, 128);
-        if (ept == 0 && ok) {
-          fence_acq_rel_sys();
+          if (!ok || t >= T) continue;
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
           for (int q = 0; q < world; ++q) {
             if (q == cv.rank) continue;
-            uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[q] + cv.L.final_flag_off);
-            for (int ch = (int)crank; ch * 16 < T; ch += p.splits)
-              st_release_sys(ff + (size_t)tile * kMaxChunks + ch, 1u);
+            uint64_t* rd = ll_result(cv, q, tile, ch) + 2 * ept;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) st_ll2(rd + 256 * i, ll_word(w[2 * i], epoch), ll_word(w[2 * i + 1], epoch));
           }
+          __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
+          reinterpret_cast<uint4*>(ydst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          reinterpret_cast<uint4*>(ydst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       } else {
-        // ---- phase 3 (everyone else): wait for the owner's results, copy them into Y
-        if (ept == 0) {
-          uint32_t* ff = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.final_flag_off);
-          bool ok = true;
-          for (int ch = (int)crank; ch * 16 < T && ok; ch += p.splits) ok = wait_flag_sys(ff + (size_t)tile * kMaxChunks + ch, 1u);
-          if (ok) {
-            for (int ch = (int)crank; ch * 16 < T; ch += p.splits) ff[(size_t)tile * kMaxChunks + ch] = 0u;
-          } else {
-            atomicOr(p.status, kStatusTimeoutPeer);
+        // ---- phase 3 (everyone else): the owner's flagged bf16 words -> Y
+        for (int ch = crank; ch * 16 < T; ch += p.splits) {
+          const int t = ch * 16 + j;
+          if (t >= T) continue;
+          const uint64_t* src = ll_result(cv, cv.rank, tile, ch) + 2 * ept;
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            w[2 * i] = w[2 * i + 1] = 0u;
+            if (ok) ok = poll_ll2(src + 256 * i, epoch, t0, w[2 * i], w[2 * i + 1]);
           }
-          tl->ok = ok ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        if (tl->ok) {
-          for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
-            const int t = ch * 16 + j;
-            if (t >= T) continue;
-            const uint4* rs = reinterpret_cast<const uint4*>(
-                reinterpret_cast<const __nv_bfloat16*>(cv.base[cv.rank] + cv.L.result_off) + (size_t)t * cv.L.max_n +
-                row0 + 16 * g8);
-            __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
-            reinterpret_cast<uint4*>(ydst)[0] = __ldcg(rs);
-            reinterpret_cast<uint4*>(ydst)[1] = __ldcg(rs + 1);
-          }
+          if (!ok) continue;
+          __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
+          reinterpret_cast<uint4*>(ydst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          reinterpret_cast<uint4*>(ydst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
+      if (!ok) atomicOr(p.status, kStatusTimeoutPeer);
     }
     if (ept == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }

@@ -164,6 +164,14 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 bit, 16 consecutive columns per thread.
+// 16 columns without waiting: issue several, then one tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(
@@ -241,6 +249,31 @@ __device__ __forceinline__ bool mbar_wait_warp_incoming(uint64_t* bar, uint32_t 
   bool ok = true;
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, nullptr) || mbar_wait(bar, parity, nullptr);
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// ------------------------------------------------------- flagged words
+// 8-byte words carrying (epoch << 32) | payload; aligned 8-byte accesses are
+// single-copy atomic, so payload and flag arrive together.
+__device__ __forceinline__ uint64_t ll_word(uint32_t payload, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | payload;
+}
+__device__ __forceinline__ void st_ll2(uint64_t* dst, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
+}
+// Poll two words until both carry `epoch`; false once the wait budget,
+// counted from t0, is spent.
+__device__ __forceinline__ bool poll_ll2(const uint64_t* src, uint32_t epoch, uint64_t t0, uint32_t& a,
+                                         uint32_t& b) {
+  while (true) {
+    uint64_t x, y;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(src) : "memory");
+    if ((uint32_t)(x >> 32) == epoch && (uint32_t)(y >> 32) == epoch) {
+      a = (uint32_t)x;
+      b = (uint32_t)y;
+      return true;
+    }
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+  }
 }
 
 // ----------------------------------------------------------------- cluster

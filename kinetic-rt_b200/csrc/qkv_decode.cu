@@ -196,12 +196,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     {
       // RoPE values of this thread's first phase-B token, fetched while the
       // main loop runs (same (token, row group) mapping as phase B).
-      const int t0 = (int)cluster_ctarank() * 16 + (ept >> 3);
-      if (t0 < T && tile < p.n_heads + p.n_kv_heads) load_rope16(p, p.tok_pos[t0], ept & 7, cs0, sn0);
+      const int t0 = (int)cluster_ctarank() * 16 + (ept & 15);
+      if (t0 < T && tile < p.n_heads + p.n_kv_heads) load_rope16(p, p.tok_pos[t0], ept >> 4, cs0, sn0);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        bias_y[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * (ept & 7) + i]) : 0.f;
-        bias_p[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * ((ept & 7) ^ 4) + i]) : 0.f;
+        bias_y[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * (ept >> 4) + i]) : 0.f;
+        bias_p[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * ((ept >> 4) ^ 4) + i]) : 0.f;
       }
     }
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
@@ -209,29 +209,43 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     tc_fence_after();
     cluster_wait();
 
-    // Park the partial token-major in the idle pipeline buffers, one 16-token
-    // chunk at a time; a chunk finished by another rank is sent to it by bulk
-    // copy as soon as it is parked.
+    // Park the partial token-major in the idle pipeline buffers, four 16-token
+    // chunks at a time; a chunk finished by another rank is sent to it by
+    // bulk copy as soon as its group is parked.
     const int rank = split;  // cluster (1, splits, 1): rank == blockIdx.y
     const int nranks = p.splits;
     float* part = reinterpret_cast<float*>(smem);
     const uint32_t part_u32 = smem_u32(part);
-    for (int c = 0; c * 16 < n_pad; ++c) {
+    const int n_chunks = n_pad / 16;
+    for (int c0 = 0; c0 < n_chunks; c0 += 4) {
+      const int nc = n_chunks - c0 < 4 ? n_chunks - c0 : 4;
       if (waited) {
-        float v[16];
-        tmem_ld16(taddr + (uint32_t)(c * 16), v);
+        uint32_t v[4][16];
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) part[(c * 16 + jj) * kYStride + r] = v[jj];
+        for (int cc = 0; cc < 4; ++cc)
+          if (cc < nc) tmem_ld16_nowait(taddr + (uint32_t)((c0 + cc) * 16), v[cc]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          if (cc < nc) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * kYStride + r] = __uint_as_float(v[cc][jj]);
+          }
       }
-      const int owner = c % nranks;
-      if (owner != rank) {
+      bool remote = false;
+      for (int cc = 0; cc < nc; ++cc) remote |= (c0 + cc) % nranks != rank;
+      if (remote) {
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (ept == 0) {
-          const int slot = recv_slot(c / nranks, nranks, owner, rank);
-          bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)owner),
-                               part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
-                               map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)owner));
+          for (int cc = 0; cc < nc; ++cc) {
+            const int c = c0 + cc, owner = c % nranks;
+            if (owner == rank) continue;
+            const int slot = recv_slot(c / nranks, nranks, owner, rank);
+            bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)owner),
+                                 part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
+                                 map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)owner));
+          }
         }
       }
     }
@@ -240,7 +254,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
     // ------------------------------------------------ finish the owned chunks
     // thread (j, g8) owns token c*16 + j and rows 16*g8 .. +15 of chunk c.
-    const int j = ept >> 3, g8 = ept & 7;
+    const int j = ept & 15, g8 = ept >> 4;  // 8 consecutive lanes: 8 tokens, one row group (no bank conflicts)
     const bool rot = tile < p.n_heads + p.n_kv_heads;
     const int gp = g8 ^ 4;
     const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
@@ -269,21 +283,30 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           y[i] = bias_y[i];
           yp[i] = bias_p[i];
         }
-        // partials summed in rank order
+        // partials summed in rank order; two ranks per round with all their
+        // loads issued before the first add
         const int oc = c / nranks;
-        for (int q = 0; q < nranks; ++q) {
-          const float* src = q == rank ? part + t * kYStride
-                                       : recv + (size_t)recv_slot(oc, nranks, rank, q) * (kChunkBytes / 4) +
-                                             (size_t)j * kYStride;
-          float4 a[4], b[4];
+        for (int q0 = 0; q0 < nranks; q0 += 2) {
+          float4 a[2][4], b[2][4];
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) a[k4] = reinterpret_cast<const float4*>(src + 16 * g8)[k4];
-          if (rot) {
+          for (int qq = 0; qq < 2; ++qq) {
+            const int q = q0 + qq < nranks ? q0 + qq : q0;
+            const float* src = q == rank ? part + t * kYStride
+                                         : recv + (size_t)recv_slot(oc, nranks, rank, q) * (kChunkBytes / 4) +
+                                               (size_t)j * kYStride;
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) b[k4] = reinterpret_cast<const float4*>(src + 16 * gp)[k4];
+            for (int k4 = 0; k4 < 4; ++k4) a[qq][k4] = reinterpret_cast<const float4*>(src + 16 * g8)[k4];
+            if (rot) {
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4) b[qq][k4] = reinterpret_cast<const float4*>(src + 16 * gp)[k4];
+            }
           }
-          add_f4x4(y, a);
-          if (rot) add_f4x4(yp, b);
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            if (q0 + qq >= nranks) break;
+            add_f4x4(y, a[qq]);
+            if (rot) add_f4x4(yp, b[qq]);
+          }
         }
         store_rows16(p, tile, t, g8, pos, tl->slot[t], y, yp, cs, sn);
       }

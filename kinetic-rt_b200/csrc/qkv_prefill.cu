@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const int gt = ept & 127;
     const int q4 = warp & 3;            // TMEM lane quadrant of this warp
     const int r = q4 * 32 + lane;       // accumulator row
-    const int j = gt >> 3, g8 = gt & 7; // phase-B token / row group
+    const int j = gt & 15, g8 = gt >> 4; // phase-B token / row group (8 lanes: 8 tokens, no bank conflicts)
     const int bar_grp = 1 + grp;        // 128-thread barrier of this group
     float* ybuf = ybufs + grp * kYBufFloats;
     pdl_wait();
