@@ -332,14 +332,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) acc[i] = 0.f;
           for (int q = 0; q < world; ++q) {
-            const uint64_t* src = ll_stage(cv, cv.rank, q, tile, ch) + 2 * ept;
+            uint32_t u[16];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              uint32_t u0 = 0, u1 = 0;
-              if (ok) ok = poll_ll2(src + 256 * i, epoch, t0, u0, u1);
-              acc[2 * i] += __uint_as_float(u0);
-              acc[2 * i + 1] += __uint_as_float(u1);
-            }
+            for (int i = 0; i < 16; ++i) u[i] = 0u;
+            if (ok) ok = poll_ll2_batch<8>(ll_stage(cv, cv.rank, q, tile, ch) + 2 * ept, 256, epoch, t0, u);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(u[i]);
           }
           if (!ok || t >= T) continue;
           uint32_t w[8];
@@ -360,13 +358,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int ch = crank; ch * 16 < T; ch += p.splits) {
           const int t = ch * 16 + j;
           if (t >= T) continue;
-          const uint64_t* src = ll_result(cv, cv.rank, tile, ch) + 2 * ept;
           uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            w[2 * i] = w[2 * i + 1] = 0u;
-            if (ok) ok = poll_ll2(src + 256 * i, epoch, t0, w[2 * i], w[2 * i + 1]);
-          }
+          for (int i = 0; i < 8; ++i) w[i] = 0u;
+          if (ok) ok = poll_ll2_batch<4>(ll_result(cv, cv.rank, tile, ch) + 2 * ept, 256, epoch, t0, w);
           if (!ok) continue;
           __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
           reinterpret_cast<uint4*>(ydst)[0] = make_uint4(w[0], w[1], w[2], w[3]);

@@ -276,6 +276,36 @@ __device__ __forceinline__ bool poll_ll2(const uint64_t* src, uint32_t epoch, ui
   }
 }
 
+// Poll N word pairs at src + stride * i (i < N) until every word carries
+// `epoch`, all N loads issued together per round so a round costs one memory
+// latency; out[2i], out[2i+1] receive the payloads.  False once the wait
+// budget, counted from t0, is spent.
+template <int N>
+__device__ __forceinline__ bool poll_ll2_batch(const uint64_t* src, int stride, uint32_t epoch, uint64_t t0,
+                                               uint32_t* out) {
+  while (true) {
+    uint64_t x[N], y[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];"
+                   : "=l"(x[i]), "=l"(y[i])
+                   : "l"(src + (size_t)stride * i)
+                   : "memory");
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) all = all && (uint32_t)(x[i] >> 32) == epoch && (uint32_t)(y[i] >> 32) == epoch;
+    if (all) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        out[2 * i] = (uint32_t)x[i];
+        out[2 * i + 1] = (uint32_t)y[i];
+      }
+      return true;
+    }
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+  }
+}
+
 // ----------------------------------------------------------------- cluster
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
