@@ -372,9 +372,6 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     p.kc = cfg.kc;
     p.stages = cfg.stages;
     p.splits = cfg.splits;
-    if (p.comm.world > 1 && tiles * p.splits > kMaxEpochCtas)
-      return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: %d CTAs exceed the %d launch counters", tiles * p.splits,
-                       kMaxEpochCtas);
     int cols = 32;
     while (cols < p.n_pad) cols <<= 1;
     p.tmem_cols = cols;

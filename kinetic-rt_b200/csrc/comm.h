@@ -17,7 +17,6 @@ constexpr int kMaxWorld = 8;
 constexpr int kArMaxCtas = 64;     // CTAs of the standalone allreduce
 constexpr int kChunkTokens = 16;   // token granularity of the fused exchange
 constexpr int kMaxChunks = 16;     // 256 tokens per launch
-constexpr int kMaxEpochCtas = 4096;  // CTAs of one fused launch with a launch counter
 
 struct CommLayout {
   int world, max_n, tiles;
@@ -27,16 +26,18 @@ struct CommLayout {
   size_t final_flag_off;   // u32 [tiles][kMaxChunks]
   size_t ar_part_off;      // u32 [kArMaxCtas][kMaxWorld]
   size_t ar_final_off;     // u32 [kMaxWorld][kArMaxCtas]
-  // Fused GEMM + allreduce exchange in flagged words: every 8-byte word is
-  // (launch epoch << 32) | 32 payload bits, written with one 8-byte store,
-  // so a reader that sees the current epoch in a word also sees its payload
-  // and no fence or separate flag is needed.
+  // Fused GEMM + allreduce exchange in flagged 8-byte words, each written
+  // with one 8-byte store and carrying the epoch of its (tile, chunk), so a
+  // reader that sees the current epoch in a word also sees its payload and
+  // no fence or separate flag is needed:
+  //   stage words  (epoch << 48) | two 24-bit floats (fp32 rounded at bit 8)
+  //   result words (epoch << 32) | bf16x2
   // Both areas hold per-chunk slots laid out [word pair][finishing thread]
   // (16 bytes per thread and pair), so a warp's store covers 512
   // contiguous bytes.
-  size_t ll_stage_off;     // [world (source)][owned tiles][kMaxChunks][8 pairs][128 threads] fp32 payload
+  size_t ll_stage_off;     // [world (source)][owned tiles][kMaxChunks][4 pairs][128 threads] 2 x f24 payload
   size_t ll_result_off;    // [tiles][kMaxChunks][4 pairs][128 threads]                       bf16x2 payload
-  size_t epoch_off;        // u32 [kMaxEpochCtas] launches seen by each CTA index
+  size_t epoch_off;        // u32 [tiles][kMaxChunks] uses of each (tile, chunk), in 1..65535
   int owned_tiles;         // ceil(tiles / world): tile t is reduced by rank t % world
   size_t total;
 };
@@ -55,9 +56,9 @@ inline CommLayout comm_layout(int world, int max_n) {
   L.ar_final_off = up(L.ar_part_off + (size_t)kArMaxCtas * kMaxWorld * 4);
   L.owned_tiles = (L.tiles + world - 1) / world;
   L.ll_stage_off = up(L.ar_final_off + (size_t)kMaxWorld * kArMaxCtas * 4);
-  L.ll_result_off = up(L.ll_stage_off + (size_t)world * L.owned_tiles * kMaxChunks * 16 * 128 * 8);
+  L.ll_result_off = up(L.ll_stage_off + (size_t)world * L.owned_tiles * kMaxChunks * 4 * 128 * 16);
   L.epoch_off = up(L.ll_result_off + (size_t)L.tiles * kMaxChunks * 4 * 128 * 16);
-  L.total = up(L.epoch_off + (size_t)kMaxEpochCtas * 4);
+  L.total = up(L.epoch_off + (size_t)L.tiles * kMaxChunks * 4);
   return L;
 }
 

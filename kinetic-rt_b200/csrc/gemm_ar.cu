@@ -15,21 +15,21 @@
 // values of this rank's partial product.
 //
 // Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1),
-// in flagged 8-byte words ((launch epoch << 32) | payload, one store each),
+// in flagged 8-byte words (epoch and payload in one store each),
 // so that no memory fence and no separate flag is on the path:
-//   1. reduce-scatter: the partial chunk (16 tokens x 128 features, fp32) is
-//      stored into the owner rank's stage [src][tile / world][chunk]
-//      (owner = tile % world);
+//   1. reduce-scatter: the partial chunk (16 tokens x 128 features, fp32
+//      rounded to 24-bit floats with a 15-bit mantissa) is stored into the
+//      owner rank's stage [src][tile / world][chunk] (owner = tile % world);
 //   2. the owner's CTA for the same chunk polls the words of all `world`
 //      ranks, sums the partials in rank order (so every rank ends with
 //      bit-identical values), writes the bf16 result to its own Y and, as
 //      flagged bf16x2 words, into every peer's result area;
 //   3. every other rank's CTA for that chunk polls those words and copies
 //      them into Y.
-// The epoch of a launch is a per-CTA-index launch counter kept in the
-// communicator's own buffer, identical on all ranks because all ranks run
-// the same launches; stale words of an earlier launch never match, so the
-// protocol needs no reset and replays from a CUDA graph.  A slot is only
+// The epoch of a (tile, chunk) is its use counter kept in the communicator's
+// own buffer, identical on all ranks because all ranks run the same
+// launches; a slot holds at most the previous use's words, which never
+// match, so the protocol needs no reset and replays from a CUDA graph.  A slot is only
 // rewritten by a launch that the reader's progress already allowed.  All
 // polls are bounded (status bit 16).
 #include <cstdint>
@@ -52,7 +52,7 @@ struct GemmSmemTail {
   uint64_t recv;  // completes when the other ranks' partials of the owned chunks have arrived
   uint32_t tmem_base;
   int abort;
-  uint32_t epoch;
+  uint32_t epoch[kMaxChunks];  // epoch of each owned chunk (fused allreduce)
   int pad;
 };
 
@@ -77,7 +77,7 @@ __device__ __forceinline__ void gemm_fail(const GemmArParams& p, GemmSmemTail* t
 // slot + 2 * (i * 128 + ept).
 __device__ __forceinline__ uint64_t* ll_stage(const CommView& cv, int holder, int src, int tile, int ch) {
   return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_stage_off) +
-         (((size_t)src * cv.L.owned_tiles + tile / cv.world) * kMaxChunks + ch) * (8 * 128 * 2);
+         (((size_t)src * cv.L.owned_tiles + tile / cv.world) * kMaxChunks + ch) * (4 * 128 * 2);
 }
 __device__ __forceinline__ uint64_t* ll_result(const CommView& cv, int holder, int tile, int ch) {
   return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_result_off) +
@@ -257,19 +257,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int owner = tile % world;
     const float* recv = reinterpret_cast<const float*>(recv_smem);
     pdl_wait();  // Y and the exchange buffers may still be in use by the previous kernel
-    // Launch epoch of this CTA index: the same on every rank, since every
-    // rank runs the same launches; it tags this launch's flagged words.
-    uint32_t epoch = 0;
+    // Epoch of each (tile, chunk) this CTA finishes: its use count in 1..65535,
+    // the same on every rank since every rank runs the same launches.  A slot
+    // of the exchange only ever holds this launch's words or the previous
+    // use's (epoch - 1), never a matching stale word.
     if (world > 1) {
       if (ept == 0) {
-        uint32_t* ctr =
-            reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.epoch_off) + (blockIdx.y * gridDim.x + blockIdx.x);
-        const uint32_t e = __ldcg(ctr) + 1u;
-        *ctr = e;
-        tl->epoch = e;
+        uint32_t* ctr = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.epoch_off) + (size_t)tile * kMaxChunks;
+        for (int ch = crank, oc = 0; ch * 16 < T; ch += p.splits, ++oc) {
+          uint32_t e = __ldcg(ctr + ch) + 1u;
+          if (e > 65535u) e = 1u;
+          ctr[ch] = e;
+          tl->epoch[oc] = e;
+        }
       }
       named_bar_sync(1, 128);
-      epoch = tl->epoch;
     }
     // ---- phase 1: this rank's partial of every chunk -> Y (one rank) or the owner's staging slot
     for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
@@ -312,12 +314,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           reinterpret_cast<uint4*>(ydst)[1] = b;
         }
       } else {
-        // one flagged fp32 word per value into the owner's stage (local when this rank owns the tile)
+        // flagged words of two 24-bit floats into the owner's stage (local
+        // when this rank owns the tile)
+        const uint32_t epoch = tl->epoch[ch / nranks];
         uint64_t* dst = ll_stage(cv, owner, cv.rank, tile, ch) + 2 * ept;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          st_ll2(dst + 256 * i, ll_word(__float_as_uint(y[2 * i]), epoch),
-                 ll_word(__float_as_uint(y[2 * i + 1]), epoch));
+        for (int i = 0; i < 4; ++i)
+          st_ll2(dst + 256 * i, f24_pair_word(y[4 * i], y[4 * i + 1], epoch),
+                 f24_pair_word(y[4 * i + 2], y[4 * i + 3], epoch));
       }
     }
     if (world > 1) {
@@ -331,13 +335,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float acc[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+          const uint32_t epoch = tl->epoch[ch / nranks];
           for (int q = 0; q < world; ++q) {
-            uint32_t u[16];
+            uint64_t u[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) u[i] = 0u;
-            if (ok) ok = poll_ll2_batch<8>(ll_stage(cv, cv.rank, q, tile, ch) + 2 * ept, 256, epoch, t0, u);
+            for (int i = 0; i < 8; ++i) u[i] = 0u;
+            if (ok) ok = poll_words_batch<4, 48>(ll_stage(cv, cv.rank, q, tile, ch) + 2 * ept, 256, epoch, t0, u);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(u[i]);
+            for (int i = 0; i < 8; ++i) {
+              const float2 v = f24_pair_unpack(u[i]);
+              acc[2 * i] += v.x;
+              acc[2 * i + 1] += v.y;
+            }
           }
           if (!ok || t >= T) continue;
           uint32_t w[8];
@@ -361,7 +370,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint32_t w[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[i] = 0u;
-          if (ok) ok = poll_ll2_batch<4>(ll_result(cv, cv.rank, tile, ch) + 2 * ept, 256, epoch, t0, w);
+          if (ok) ok = poll_ll2_batch<4>(ll_result(cv, cv.rank, tile, ch) + 2 * ept, 256, tl->epoch[ch / nranks], t0, w);
           if (!ok) continue;
           __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
           reinterpret_cast<uint4*>(ydst)[0] = make_uint4(w[0], w[1], w[2], w[3]);

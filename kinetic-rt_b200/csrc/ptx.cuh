@@ -276,6 +276,51 @@ __device__ __forceinline__ bool poll_ll2(const uint64_t* src, uint32_t epoch, ui
   }
 }
 
+// 24-bit float: fp32 rounded to nearest-even at mantissa bit 8 (sign,
+// 8-bit exponent, 15-bit mantissa); two of them and a 16-bit epoch fill one
+// flagged word: (epoch << 48) | (b << 24) | a.
+__device__ __forceinline__ uint64_t f24_pair_word(float a, float b, uint32_t epoch16) {
+  auto f24 = [](float v) -> uint64_t {
+    const uint32_t u = __float_as_uint(v);
+    return (uint64_t)((u + 0x7Fu + ((u >> 8) & 1u)) >> 8) & 0xFFFFFFull;
+  };
+  return ((uint64_t)epoch16 << 48) | (f24(b) << 24) | f24(a);
+}
+__device__ __forceinline__ float2 f24_pair_unpack(uint64_t w) {
+  return make_float2(__uint_as_float((uint32_t)(w & 0xFFFFFFull) << 8),
+                     __uint_as_float((uint32_t)((w >> 24) & 0xFFFFFFull) << 8));
+}
+
+// Poll N word pairs at src + stride * i (i < N) until every word carries
+// `epoch` in its bits [SHIFT, 64), all N loads issued together per round so a
+// round costs one memory latency; out[2i], out[2i+1] receive the words.
+// False once the wait budget, counted from t0, is spent.
+template <int N, int SHIFT>
+__device__ __forceinline__ bool poll_words_batch(const uint64_t* src, int stride, uint32_t epoch, uint64_t t0,
+                                                 uint64_t* out) {
+  while (true) {
+    uint64_t x[N], y[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];"
+                   : "=l"(x[i]), "=l"(y[i])
+                   : "l"(src + (size_t)stride * i)
+                   : "memory");
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) all = all && (uint32_t)(x[i] >> SHIFT) == epoch && (uint32_t)(y[i] >> SHIFT) == epoch;
+    if (all) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        out[2 * i] = x[i];
+        out[2 * i + 1] = y[i];
+      }
+      return true;
+    }
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+  }
+}
+
 // Poll N word pairs at src + stride * i (i < N) until every word carries
 // `epoch`, all N loads issued together per round so a round costs one memory
 // latency; out[2i], out[2i+1] receive the payloads.  False once the wait
