@@ -27,11 +27,12 @@ cudaError_t launch_qkv_rope_generic(const GenericArgs& a, int dtype, int freqs_d
 size_t generic_smem_bytes(int d_model, int n_out);
 
 // qkv_decode.cu
-size_t decode_smem_bytes(int stages, int n_pad, int kc, int splits);
-cudaError_t launch_qkv_rope_decode(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
-                                   int tiles, cudaStream_t stream);
+// tile_m = 128 (one head per tile) or 64 (half a head per tile)
+size_t decode_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits);
+cudaError_t launch_qkv_rope_decode(int tile_m, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                                   const PagedParams& p, int tiles, cudaStream_t stream);
 
-int decode_max_active_clusters(int splits, int n_pad, int stages, int kc);
+int decode_max_active_clusters(int tile_m, int splits, int n_pad, int stages, int kc);
 
 // qkv_prep.cu
 cudaError_t launch_qkv_prep(const PagedParams& p, cudaStream_t stream);
@@ -43,9 +44,9 @@ cudaError_t launch_qkv_rope_prefill(const CUtensorMap& tmap_w, const CUtensorMap
 
 // gemm_ar.cu
 struct GemmArParams;
-size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc, int splits);
-int gemm_ar_max_active_clusters(int splits, int n_pad, int stages, int kc);
-cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmArParams& p,
-                                       int tiles, cudaStream_t stream);
+size_t gemm_ar_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits);
+int gemm_ar_max_active_clusters(int tile_m, int splits, int n_pad, int stages, int kc);
+cudaError_t launch_rowparallel_gemm_ar(int tile_m, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                                       const GemmArParams& p, int tiles, cudaStream_t stream);
 
 }  // namespace krt

@@ -15,6 +15,7 @@
 // result to everyone.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -275,19 +276,24 @@ extern "C" int krt_allreduce(krt_comm* c, const void* send, void* recv, size_t c
 // ------------------------------------------------------ fused GEMM + allreduce
 namespace {
 
-int gemm_stages(int n_pad, int kc, int splits) {
+int env_tile_m(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+int gemm_stages(int tile_m, int n_pad, int kc, int splits) {
   for (int st = kMaxStages; st >= 1; --st)
-    if (gemm_ar_smem_bytes(st, n_pad, kc, splits) <= 227 * 1024) return st;
+    if (gemm_ar_smem_bytes(tile_m, st, n_pad, kc, splits) <= 227 * 1024) return st;
   return 0;
 }
 
 // Box depth with the most weight bytes in flight.
-int gemm_kc(int num_kb, int n_pad, int splits) {
+int gemm_kc(int tile_m, int num_kb, int n_pad, int splits) {
   int best = 1;
   size_t best_bytes = 0;
   for (int kc = 4; kc >= 1; kc >>= 1) {
     if (num_kb % kc != 0) continue;
-    const size_t bytes = (size_t)gemm_stages(n_pad, kc, splits) * kc * 16384;
+    const size_t bytes = (size_t)gemm_stages(tile_m, n_pad, kc, splits) * kc * tile_m * 128;
     if (bytes > best_bytes) {
       best_bytes = bytes;
       best = kc;
@@ -297,30 +303,37 @@ int gemm_kc(int num_kb, int n_pad, int splits) {
 }
 
 struct GemmCfg {
-  int kc, stages, splits;
+  int tile_m, tiles, kc, stages, splits;
 };
 
-// Split-K factor = cluster size: as many splits as fit (tiles * splits <=
-// #SMs, at most 8) while every cluster can be resident at once.
-GemmCfg gemm_config(int tiles, int num_kb, int n_pad) {
+// Tile height 128; 64 (twice the tiles, half the K splits and half the
+// exchange per split, but every tile re-reads X) is slower at every decode
+// shape measured on B200 (K = 512 .. 14336, N = 4096, 64 tokens) and only
+// runs when KRT_GEMM_TILE_M=64 asks for it.  Split-K factor = cluster size: as many splits
+// as fit (tiles * splits <= #SMs, at most 8) while every cluster can be
+// resident at once.
+GemmCfg gemm_config(int n_out, int num_kb, int n_pad) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, int, int>, GemmCfg> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, tiles, num_kb, n_pad);
+  const auto key = std::make_tuple(dev, n_out, num_kb, n_pad);
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  GemmCfg cfg{1, 1, 1};
+  int tile_m = env_tile_m("KRT_GEMM_TILE_M", 128);
+  if (tile_m != 64) tile_m = 128;
+  const int tiles = n_out / tile_m;
+  GemmCfg cfg{tile_m, tiles, 1, 1, 1};
   int s = device_sm_count() / tiles;
   if (s > 8) s = 8;
   if (s < 1) s = 1;
   for (; s >= 1; --s) {
-    const int kc = gemm_kc(num_kb, n_pad, s);
-    const int st = gemm_stages(n_pad, kc, s);
+    const int kc = gemm_kc(tile_m, num_kb, n_pad, s);
+    const int st = gemm_stages(tile_m, n_pad, kc, s);
     if (st < 1 || s > num_kb / kc) continue;
-    cfg = GemmCfg{kc, st, s};
-    if (s == 1 || gemm_ar_max_active_clusters(s, n_pad, st, kc) >= tiles) break;
+    cfg = GemmCfg{tile_m, tiles, kc, st, s};
+    if (s == 1 || gemm_ar_max_active_clusters(tile_m, s, n_pad, st, kc) >= tiles) break;
   }
   cache[key] = cfg;
   return cfg;
@@ -357,7 +370,6 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     p.comm.world = 1;
     p.comm.rank = 0;
   }
-  const int tiles = a->n_out / 128;
   const int num_kb = a->k_local / 64;
   p.n_out = a->n_out;
   p.k_local = a->k_local;
@@ -368,7 +380,7 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
     p.num_tokens = T;
     p.n_pad = (T + 15) / 16 * 16;
-    const GemmCfg cfg = gemm_config(tiles, num_kb, p.n_pad);
+    const GemmCfg cfg = gemm_config(a->n_out, num_kb, p.n_pad);
     p.kc = cfg.kc;
     p.stages = cfg.stages;
     p.splits = cfg.splits;
@@ -379,12 +391,12 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
     CUtensorMap tmap_w, tmap_x;
     int rc = make_tmap_bf16_3d(&tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local, (uint64_t)a->k_local,
-                               128, (uint32_t)p.kc);
+                               (uint32_t)cfg.tile_m, (uint32_t)p.kc);
     if (rc) return rc;
     rc = make_tmap_bf16_3d(&tmap_x, xp, (uint64_t)T, (uint64_t)a->k_local, (uint64_t)a->x_stride, (uint32_t)p.n_pad,
                            (uint32_t)p.kc);
     if (rc) return rc;
-    cudaError_t e = launch_rowparallel_gemm_ar(tmap_w, tmap_x, p, tiles, s);
+    cudaError_t e = launch_rowparallel_gemm_ar(cfg.tile_m, tmap_w, tmap_x, p, cfg.tiles, s);
     if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
   }
   return clear_error();

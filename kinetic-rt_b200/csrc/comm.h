@@ -32,13 +32,14 @@ struct CommLayout {
   // no fence or separate flag is needed:
   //   stage words  (epoch << 48) | two 24-bit floats (fp32 rounded at bit 8)
   //   result words (epoch << 32) | bf16x2
-  // Both areas hold per-chunk slots laid out [word pair][finishing thread]
-  // (16 bytes per thread and pair), so a warp's store covers 512
-  // contiguous bytes.
-  size_t ll_stage_off;     // [world (source)][owned tiles][kMaxChunks][4 pairs][128 threads] 2 x f24 payload
-  size_t ll_result_off;    // [tiles][kMaxChunks][4 pairs][128 threads]                       bf16x2 payload
-  size_t epoch_off;        // u32 [tiles][kMaxChunks] uses of each (tile, chunk), in 1..65535
-  int owned_tiles;         // ceil(tiles / world): tile t is reduced by rank t % world
+  // Slots are laid out [word pair][finishing thread] (16 bytes per thread
+  // and pair), so a warp's store covers 512 contiguous bytes.  One set of
+  // areas per tile height (index 0: 128 rows, 1: 64 rows), so the slots and
+  // epochs of the two tilings never alias.
+  size_t ll_stage_off[2];   // [world (source)][owned tiles][kMaxChunks][rows/32 pairs][128 threads]
+  size_t ll_result_off[2];  // [tiles][kMaxChunks][rows/32 pairs][128 threads]
+  size_t epoch_off[2];      // u32 [tiles][kMaxChunks] uses of each (tile, chunk), in 1..65535
+  int owned_tiles[2];       // ceil(tiles / world): tile t is reduced by rank t % world
   size_t total;
 };
 
@@ -54,11 +55,18 @@ inline CommLayout comm_layout(int world, int max_n) {
   L.final_flag_off = up(L.part_flag_off + (size_t)L.tiles * kMaxChunks * kMaxWorld * 4);
   L.ar_part_off = up(L.final_flag_off + (size_t)L.tiles * kMaxChunks * 4);
   L.ar_final_off = up(L.ar_part_off + (size_t)kArMaxCtas * kMaxWorld * 4);
-  L.owned_tiles = (L.tiles + world - 1) / world;
-  L.ll_stage_off = up(L.ar_final_off + (size_t)kMaxWorld * kArMaxCtas * 4);
-  L.ll_result_off = up(L.ll_stage_off + (size_t)world * L.owned_tiles * kMaxChunks * 4 * 128 * 16);
-  L.epoch_off = up(L.ll_result_off + (size_t)L.tiles * kMaxChunks * 4 * 128 * 16);
-  L.total = up(L.epoch_off + (size_t)L.tiles * kMaxChunks * 4);
+  size_t off = up(L.ar_final_off + (size_t)kMaxWorld * kArMaxCtas * 4);
+  for (int v = 0; v < 2; ++v) {
+    const int rows = v == 0 ? 128 : 64;
+    const int tiles = max_n / rows;
+    const size_t slot = (size_t)rows * 64;  // bytes: rows/32 pairs x 128 threads x 16
+    L.owned_tiles[v] = (tiles + world - 1) / world;
+    L.ll_stage_off[v] = off;
+    L.ll_result_off[v] = up(off + (size_t)world * L.owned_tiles[v] * kMaxChunks * slot);
+    L.epoch_off[v] = up(L.ll_result_off[v] + (size_t)tiles * kMaxChunks * slot);
+    off = up(L.epoch_off[v] + (size_t)tiles * kMaxChunks * 4);
+  }
+  L.total = off;
   return L;
 }
 

@@ -8,16 +8,18 @@
 // tests/mock_rccl.h:51-62).  One launch handles up to 256 tokens.
 //
 // GEMM part (same structure as the decode QKV kernel): swap-AB, UMMA M = 128
-// output features per tile, N = padded tokens, W and X tiles by TMA in
-// {64, rows, KC} boxes, split-K across a thread-block cluster whose ranks
-// send each other their partial chunks by bulk DSMEM copy.  The finishing
-// thread (token j, features 16*g8 .. +15) of chunk `ch` then owns 16 fp32
-// values of this rank's partial product.
+// or 64 output features per tile (64 up to 128 tokens: twice the tiles, so
+// half the K splits fill the SMs and each split exchanges half the data),
+// N = padded tokens, W and X tiles by TMA in {64, rows, KC} boxes, split-K
+// across a thread-block cluster whose ranks send each other their partial
+// chunks by bulk DSMEM copy.  The finishing thread (token j, features
+// RG*g .. +RG-1, RG = rows / 8) of chunk `ch` then owns RG fp32 values of
+// this rank's partial product.
 //
 // Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1),
-// in flagged 8-byte words (epoch and payload in one store each),
-// so that no memory fence and no separate flag is on the path:
-//   1. reduce-scatter: the partial chunk (16 tokens x 128 features, fp32
+// in flagged 8-byte words (epoch and payload in one store each), so that no
+// memory fence and no separate flag is on the path:
+//   1. reduce-scatter: the partial chunk (16 tokens x rows features, fp32
 //      rounded to 24-bit floats with a 15-bit mantissa) is stored into the
 //      owner rank's stage [src][tile / world][chunk] (owner = tile % world);
 //   2. the owner's CTA for the same chunk polls the words of all `world`
@@ -29,9 +31,9 @@
 // The epoch of a (tile, chunk) is its use counter kept in the communicator's
 // own buffer, identical on all ranks because all ranks run the same
 // launches; a slot holds at most the previous use's words, which never
-// match, so the protocol needs no reset and replays from a CUDA graph.  A slot is only
-// rewritten by a launch that the reader's progress already allowed.  All
-// polls are bounded (status bit 16).
+// match, so the protocol needs no reset and replays from a CUDA graph.  A
+// slot is only rewritten by a launch that the reader's progress already
+// allowed.  All polls are bounded (status bit 16).
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -43,7 +45,6 @@
 namespace krt {
 
 constexpr int kGemmThreads = 192;
-constexpr uint32_t kGemmTileABytes = 128 * 128;
 
 struct GemmSmemTail {
   uint64_t full[kMaxStages];
@@ -57,14 +58,23 @@ struct GemmSmemTail {
 };
 
 // Pipeline buffers; after the main loop they hold the parked partial.
+template <int TM>
 __host__ __device__ inline size_t gemm_pipe_bytes(int stages, int n_pad, int kc) {
-  size_t pipe = (size_t)stages * kc * (kGemmTileABytes + (size_t)n_pad * 128);
-  if (pipe < park_area_bytes(n_pad)) pipe = park_area_bytes(n_pad);
+  size_t pipe = (size_t)stages * kc * (TileShape<TM>::kSliceBytes + (size_t)n_pad * 128);
+  const size_t park = park_area_bytes(n_pad, TileShape<TM>::kParkStride);
+  if (pipe < park) pipe = park;
   return (pipe + 127) & ~size_t(127);
 }
 
-size_t gemm_ar_smem_bytes(int stages, int n_pad, int kc, int splits) {
-  return 1024 + gemm_pipe_bytes(stages, n_pad, kc) + recv_area_bytes(n_pad, splits) + sizeof(GemmSmemTail);
+template <int TM>
+size_t gemm_ar_smem_bytes_t(int stages, int n_pad, int kc, int splits) {
+  return 1024 + gemm_pipe_bytes<TM>(stages, n_pad, kc) + recv_area_bytes(n_pad, splits, TileShape<TM>::kChunkBytes) +
+         sizeof(GemmSmemTail);
+}
+
+size_t gemm_ar_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits) {
+  return tile_m == 64 ? gemm_ar_smem_bytes_t<64>(stages, n_pad, kc, splits)
+                      : gemm_ar_smem_bytes_t<128>(stages, n_pad, kc, splits);
 }
 
 __device__ __forceinline__ void gemm_fail(const GemmArParams& p, GemmSmemTail* tl, int code) {
@@ -72,40 +82,51 @@ __device__ __forceinline__ void gemm_fail(const GemmArParams& p, GemmSmemTail* t
   tl->abort = 1;
 }
 
-// Flagged-word areas of the fused exchange (see CommLayout).
+// Flagged-word areas of the fused exchange (see CommLayout), tile height TM.
 // Slot of one chunk; the word pair i of finishing thread `ept` is at
 // slot + 2 * (i * 128 + ept).
+template <int TM>
 __device__ __forceinline__ uint64_t* ll_stage(const CommView& cv, int holder, int src, int tile, int ch) {
-  return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_stage_off) +
-         (((size_t)src * cv.L.owned_tiles + tile / cv.world) * kMaxChunks + ch) * (4 * 128 * 2);
+  constexpr int v = TM == 64 ? 1 : 0;
+  return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_stage_off[v]) +
+         (((size_t)src * cv.L.owned_tiles[v] + tile / cv.world) * kMaxChunks + ch) * (TM / 32 * 128 * 2);
 }
+template <int TM>
 __device__ __forceinline__ uint64_t* ll_result(const CommView& cv, int holder, int tile, int ch) {
-  return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_result_off) +
-         ((size_t)tile * kMaxChunks + ch) * (4 * 128 * 2);
+  constexpr int v = TM == 64 ? 1 : 0;
+  return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_result_off[v]) +
+         ((size_t)tile * kMaxChunks + ch) * (TM / 32 * 128 * 2);
 }
 
-__device__ __forceinline__ void pack16(const float* v, uint4& a, uint4& b) {
-  a = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-  b = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
-                 pack_bf16x2(v[14], v[15]));
+// RG bf16 values as RG / 8 16-byte vectors.
+template <int RG>
+__device__ __forceinline__ void store_bf16_rows(__nv_bfloat16* dst, const uint32_t* w) {
+#pragma unroll
+  for (int h = 0; h < RG / 8; ++h)
+    reinterpret_cast<uint4*>(dst)[h] = make_uint4(w[4 * h], w[4 * h + 1], w[4 * h + 2], w[4 * h + 3]);
 }
 
+template <int TM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     rowparallel_gemm_ar_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                                const GemmArParams p) {
+  using TS = TileShape<TM>;
+  constexpr int RG = TS::kRowsPerThread;  // features per finishing thread
+  constexpr int YS = TS::kParkStride;
+  constexpr int NP = RG / 4;              // 16-byte word pairs per thread in a flagged slot
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.stages;
   const int KC = p.kc;
   const int n_pad = p.n_pad;
   const uint32_t b_chunk = (uint32_t)n_pad * 128u;
-  const uint32_t a_stage = (uint32_t)KC * kGemmTileABytes;
+  const uint32_t a_stage = (uint32_t)KC * TS::kSliceBytes;
   const uint32_t b_stage = (uint32_t)KC * b_chunk;
   const uint32_t stage_bytes = a_stage + b_stage;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + (size_t)S * a_stage;
-  uint8_t* recv_smem = smem + gemm_pipe_bytes(S, n_pad, KC);
-  GemmSmemTail* tl = reinterpret_cast<GemmSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits));
+  uint8_t* recv_smem = smem + gemm_pipe_bytes<TM>(S, n_pad, KC);
+  GemmSmemTail* tl = reinterpret_cast<GemmSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits, TS::kChunkBytes));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -113,7 +134,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kc0 = (int)((long long)split * num_kc / p.splits);
   const int kc1 = (int)((long long)(split + 1) * num_kc / p.splits);
   const int nk = kc1 - kc0;
-  const int row0 = tile * 128;
+  const int row0 = tile * TM;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -126,7 +147,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbar_init();
     // the partials this CTA will receive: (splits - 1) per owned chunk
     mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
-                                         kChunkBytes);
+                                         TS::kChunkBytes);
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
@@ -170,7 +191,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(128, n_pad);
+      const uint32_t idesc = umma_idesc_bf16(TM, n_pad);
       for (int i = 0; i < nk; ++i) {
         const int s = i % S;
         const uint32_t ph = (uint32_t)(i / S) & 1u;
@@ -180,7 +201,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         for (int kc = 0; kc < KC; ++kc) {
-          const uint64_t ad = umma_desc_sw128(smem_u32(a_smem + (size_t)s * a_stage + (size_t)kc * kGemmTileABytes));
+          const uint64_t ad =
+              umma_desc_sw128(smem_u32(a_smem + (size_t)s * a_stage + (size_t)kc * TS::kSliceBytes));
           const uint64_t bd = umma_desc_sw128(smem_u32(b_smem + (size_t)s * b_stage + (size_t)kc * b_chunk));
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
@@ -192,7 +214,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;
+    // accumulator row held by this lane (M = 64: lanes 16-31 of each quarter hold none)
+    const int r = TM == 128 ? q4 * 32 + lane : (lane < 16 ? q4 * 16 + lane : -1);
     const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16);
     const int ept = threadIdx.x - 64;
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
@@ -216,12 +239,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int cc = 0; cc < 4; ++cc)
           if (cc < nc) tmem_ld16_nowait(taddr + (uint32_t)((c0 + cc) * 16), v[cc]);
         tmem_wait_ld();
+        if (r >= 0) {
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc)
-          if (cc < nc) {
+          for (int cc = 0; cc < 4; ++cc)
+            if (cc < nc) {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * kYStride + r] = __uint_as_float(v[cc][jj]);
-          }
+              for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * YS + r] = __uint_as_float(v[cc][jj]);
+            }
+        }
       }
       bool remote = false;
       for (int cc = 0; cc < nc; ++cc) remote |= (c0 + cc) % nranks != crank;
@@ -233,9 +258,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int c = c0 + cc, cowner = c % nranks;
             if (cowner == crank) continue;
             const int slot = recv_slot(c / nranks, nranks, cowner, crank);
-            bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)cowner),
-                                 part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
-                                 map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)cowner));
+            bulk_copy_to_cluster(
+                map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * TS::kChunkBytes, (uint32_t)cowner),
+                part_u32 + (uint32_t)c * TS::kChunkBytes, TS::kChunkBytes,
+                map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)cowner));
           }
         }
       }
@@ -245,11 +271,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
     if (!got && lane == 0) gemm_fail(p, tl, kStatusTimeoutCluster);
 
-    // Thread (token j, features 16*g8 .. +15) of each chunk this CTA finishes
-    // (chunks crank, crank + splits, ...).  Each cross-GPU exchange phase
-    // covers all of the CTA's chunks at once, so a launch pays two NVLink
-    // round trips.
-    const int j = ept & 15, g8 = ept >> 4;  // 8 consecutive lanes: 8 tokens, one row group (no bank conflicts)
+    // Thread (token j, features RG*g .. +RG-1) of each chunk this CTA
+    // finishes (chunks crank, crank + splits, ...); 8 consecutive lanes take
+    // 8 tokens of one feature group (no bank conflicts).  Each cross-GPU
+    // exchange phase covers all of the CTA's chunks at once, so a launch pays
+    // two NVLink round trips.
+    const int j = ept & 15, g = ept >> 4;
     const int T = p.num_tokens;
     const CommView& cv = p.comm;
     const int world = cv.world;
@@ -263,7 +290,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // use's (epoch - 1), never a matching stale word.
     if (world > 1) {
       if (ept == 0) {
-        uint32_t* ctr = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.epoch_off) + (size_t)tile * kMaxChunks;
+        uint32_t* ctr = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.epoch_off[TM == 64 ? 1 : 0]) +
+                        (size_t)tile * kMaxChunks;
         for (int ch = crank, oc = 0; ch * 16 < T; ch += p.splits, ++oc) {
           uint32_t e = __ldcg(ctr + ch) + 1u;
           if (e > 65535u) e = 1u;
@@ -273,31 +301,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       named_bar_sync(1, 128);
     }
-    // ---- phase 1: this rank's partial of every chunk -> Y (one rank) or the owner's staging slot
-    for (int ch = (int)crank; ch * 16 < T; ch += p.splits) {
+    // ---- phase 1: this rank's partial of every chunk -> Y (one rank) or the owner's stage
+    for (int ch = crank; ch * 16 < T; ch += p.splits) {
       const int t = ch * 16 + j;
-      float y[16];
+      float y[RG];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) y[i] = 0.f;
+      for (int i = 0; i < RG; ++i) y[i] = 0.f;
       // partials of the cluster ranks, summed in rank order; four ranks per
       // round with all their loads issued before the first add
       const int oc = ch / nranks;
       for (int q0 = 0; q0 < nranks; q0 += 4) {
-        float4 a[4][4];
+        float4 a[4][RG / 4];
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           const int q = q0 + qq < nranks ? q0 + qq : q0;
-          const float* src = q == crank ? part + t * kYStride + 16 * g8
-                                        : recv + (size_t)recv_slot(oc, nranks, crank, q) * (kChunkBytes / 4) +
-                                              (size_t)j * kYStride + 16 * g8;
+          const float* src = q == crank ? part + t * YS + RG * g
+                                        : recv + (size_t)recv_slot(oc, nranks, crank, q) * (TS::kChunkBytes / 4) +
+                                              (size_t)j * YS + RG * g;
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) a[qq][k4] = reinterpret_cast<const float4*>(src)[k4];
+          for (int k4 = 0; k4 < RG / 4; ++k4) a[qq][k4] = reinterpret_cast<const float4*>(src)[k4];
         }
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           if (q0 + qq >= nranks) break;
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
+          for (int k4 = 0; k4 < RG / 4; ++k4) {
             y[4 * k4 + 0] += a[qq][k4].x;
             y[4 * k4 + 1] += a[qq][k4].y;
             y[4 * k4 + 2] += a[qq][k4].z;
@@ -307,19 +335,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (world == 1) {
         if (alive && t < T) {
-          uint4 a, b;
-          pack16(y, a, b);
-          __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
-          reinterpret_cast<uint4*>(ydst)[0] = a;
-          reinterpret_cast<uint4*>(ydst)[1] = b;
+          uint32_t w[RG / 2];
+#pragma unroll
+          for (int i = 0; i < RG / 2; ++i) w[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
+          store_bf16_rows<RG>(p.y + (size_t)t * p.y_stride + row0 + RG * g, w);
         }
       } else {
         // flagged words of two 24-bit floats into the owner's stage (local
         // when this rank owns the tile)
         const uint32_t epoch = tl->epoch[ch / nranks];
-        uint64_t* dst = ll_stage(cv, owner, cv.rank, tile, ch) + 2 * ept;
+        uint64_t* dst = ll_stage<TM>(cv, owner, cv.rank, tile, ch) + 2 * ept;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < NP; ++i)
           st_ll2(dst + 256 * i, f24_pair_word(y[4 * i], y[4 * i + 1], epoch),
                  f24_pair_word(y[4 * i + 2], y[4 * i + 3], epoch));
       }
@@ -332,49 +359,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // order; the bf16 result goes to Y and, as flagged words, to every peer
         for (int ch = crank; ch * 16 < T; ch += p.splits) {
           const int t = ch * 16 + j;
-          float acc[16];
+          float acc[RG];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+          for (int i = 0; i < RG; ++i) acc[i] = 0.f;
           const uint32_t epoch = tl->epoch[ch / nranks];
           for (int q = 0; q < world; ++q) {
-            uint64_t u[8];
+            uint64_t u[RG / 2];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) u[i] = 0u;
-            if (ok) ok = poll_words_batch<4, 48>(ll_stage(cv, cv.rank, q, tile, ch) + 2 * ept, 256, epoch, t0, u);
+            for (int i = 0; i < RG / 2; ++i) u[i] = 0u;
+            if (ok) ok = poll_words_batch<NP, 48>(ll_stage<TM>(cv, cv.rank, q, tile, ch) + 2 * ept, 256, epoch, t0, u);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < RG / 2; ++i) {
               const float2 v = f24_pair_unpack(u[i]);
               acc[2 * i] += v.x;
               acc[2 * i + 1] += v.y;
             }
           }
           if (!ok || t >= T) continue;
-          uint32_t w[8];
+          uint32_t w[RG / 2];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
+          for (int i = 0; i < RG / 2; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
           for (int q = 0; q < world; ++q) {
             if (q == cv.rank) continue;
-            uint64_t* rd = ll_result(cv, q, tile, ch) + 2 * ept;
+            uint64_t* rd = ll_result<TM>(cv, q, tile, ch) + 2 * ept;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) st_ll2(rd + 256 * i, ll_word(w[2 * i], epoch), ll_word(w[2 * i + 1], epoch));
+            for (int i = 0; i < NP; ++i) st_ll2(rd + 256 * i, ll_word(w[2 * i], epoch), ll_word(w[2 * i + 1], epoch));
           }
-          __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
-          reinterpret_cast<uint4*>(ydst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          reinterpret_cast<uint4*>(ydst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          store_bf16_rows<RG>(p.y + (size_t)t * p.y_stride + row0 + RG * g, w);
         }
       } else {
         // ---- phase 3 (everyone else): the owner's flagged bf16 words -> Y
         for (int ch = crank; ch * 16 < T; ch += p.splits) {
           const int t = ch * 16 + j;
           if (t >= T) continue;
-          uint32_t w[8];
+          uint32_t w[RG / 2];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = 0u;
-          if (ok) ok = poll_ll2_batch<4>(ll_result(cv, cv.rank, tile, ch) + 2 * ept, 256, tl->epoch[ch / nranks], t0, w);
+          for (int i = 0; i < RG / 2; ++i) w[i] = 0u;
+          if (ok)
+            ok = poll_ll2_batch<NP>(ll_result<TM>(cv, cv.rank, tile, ch) + 2 * ept, 256, tl->epoch[ch / nranks], t0,
+                                    w);
           if (!ok) continue;
-          __nv_bfloat16* ydst = p.y + (size_t)t * p.y_stride + row0 + 16 * g8;
-          reinterpret_cast<uint4*>(ydst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          reinterpret_cast<uint4*>(ydst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          store_bf16_rows<RG>(p.y + (size_t)t * p.y_stride + row0 + RG * g, w);
         }
       }
       if (!ok) atomicOr(p.status, kStatusTimeoutPeer);
@@ -391,11 +416,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmArParams& p,
-                                       int tiles, cudaStream_t stream) {
-  const size_t smem = gemm_ar_smem_bytes(p.stages, p.n_pad, p.kc, p.splits);
+template <int TM>
+static cudaError_t launch_gemm_ar_t(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmArParams& p,
+                                    int tiles, cudaStream_t stream) {
+  const size_t smem = gemm_ar_smem_bytes_t<TM>(p.stages, p.n_pad, p.kc, p.splits);
   cudaError_t e =
-      cudaFuncSetAttribute(rowparallel_gemm_ar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(rowparallel_gemm_ar_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, p.splits, 1);
@@ -411,12 +437,19 @@ cudaError_t launch_rowparallel_gemm_ar(const CUtensorMap& tmap_w, const CUtensor
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, rowparallel_gemm_ar_kernel, tmap_w, tmap_x, p);
+  return cudaLaunchKernelEx(&cfg, rowparallel_gemm_ar_kernel<TM>, tmap_w, tmap_x, p);
 }
 
-int gemm_ar_max_active_clusters(int splits, int n_pad, int stages, int kc) {
-  const size_t smem = gemm_ar_smem_bytes(stages, n_pad, kc, splits);
-  if (cudaFuncSetAttribute(rowparallel_gemm_ar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+cudaError_t launch_rowparallel_gemm_ar(int tile_m, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                                       const GemmArParams& p, int tiles, cudaStream_t stream) {
+  return tile_m == 64 ? launch_gemm_ar_t<64>(tmap_w, tmap_x, p, tiles, stream)
+                      : launch_gemm_ar_t<128>(tmap_w, tmap_x, p, tiles, stream);
+}
+
+template <int TM>
+static int gemm_ar_max_active_clusters_t(int splits, int n_pad, int stages, int kc) {
+  const size_t smem = gemm_ar_smem_bytes_t<TM>(stages, n_pad, kc, splits);
+  if (cudaFuncSetAttribute(rowparallel_gemm_ar_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return 0;
   cudaLaunchConfig_t cfg = {};
@@ -431,11 +464,16 @@ int gemm_ar_max_active_clusters(int splits, int n_pad, int stages, int kc) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, rowparallel_gemm_ar_kernel, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, rowparallel_gemm_ar_kernel<TM>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return n;
+}
+
+int gemm_ar_max_active_clusters(int tile_m, int splits, int n_pad, int stages, int kc) {
+  return tile_m == 64 ? gemm_ar_max_active_clusters_t<64>(splits, n_pad, stages, kc)
+                      : gemm_ar_max_active_clusters_t<128>(splits, n_pad, stages, kc);
 }
 
 }  // namespace krt

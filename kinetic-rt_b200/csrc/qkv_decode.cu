@@ -5,24 +5,28 @@
 // stream (50 MB for Llama-3-8B shapes) dominates, so the kernel is HBM-bound
 // and is laid out to keep every SM streaming weights:
 //
-//   * swap-AB: the UMMA M dimension is 128 weight rows (one head of Q, K or
-//     V), N is the padded token count, so the accumulator of a head is one
-//     128-lane x n_pad-column TMEM tile;
-//   * split-K over gridDim.y so that (heads x splits) ~ #SMs, the splits of a
-//     head forming one thread-block cluster: after the main loop every CTA
-//     parks its fp32 partial tile in its own shared memory, and each CTA
-//     finalises a share of the 16-token chunks by summing the partials of
-//     all CTAs of the cluster over DSMEM in rank order (deterministic, no
-//     global workspace traffic, the finishing work spread over the cluster);
+//   * swap-AB: the UMMA M dimension is a tile of weight rows, N is the padded
+//     token count.  A tile is a whole head (M = 128) or, for up to 128
+//     tokens, half a head (M = 64: rows 32*h .. +31 and 64 + 32*h .. +31 of
+//     the head, h = 0, 1, fetched by one 5-D TMA box), which keeps each
+//     row's rotate-half partner (r ^ 64) in the same tile and doubles the
+//     tile count, so fewer K splits (less exchange) fill the SMs;
+//   * split-K over gridDim.y so that (tiles x splits) ~ #SMs, the splits of a
+//     tile forming one thread-block cluster: after the main loop every CTA
+//     parks its fp32 partial token-major in its idle pipeline buffers and
+//     bulk-copies the 16-token chunks that other ranks finish into their
+//     receive areas (cp.async.bulk shared::cta -> shared::cluster, completing
+//     the receiver's mbarrier); chunk c is finished by rank c % splits from
+//     its own shared memory, partials summed in rank order (deterministic);
 //   * the normalised activations x_hat and the per-token pool slots come from
 //     qkv_prep_kernel, launched just before with programmatic dependent
 //     launch: the W tiles of the first pipeline stages are requested before
 //     griddepcontrol.wait, so the weight stream starts while the prep kernel
 //     still runs;
-//   * the finishing thread (token, 16-row group) reads its rows and their
-//     rotate-half partner rows (r ^ 64) from the parked partials, applies
-//     bias and RoPE in fp32 and writes Q densely and K/V into the paged pool
-//     with 16-byte stores (store_rows16).
+//   * the finishing thread (token, row group) applies bias and RoPE in fp32
+//     and writes Q densely and K/V into the paged pool with 16-byte stores
+//     (store_rows_n); its first token's RoPE values and its bias are fetched
+//     while the main loop runs.
 //
 // Warp roles (192 threads): warp 0 = TMA producer (W and x_hat tiles),
 // warp 1 = TMEM owner + single-thread UMMA issuer, warps 2-5 = epilogue
@@ -37,7 +41,6 @@
 namespace krt {
 
 constexpr int kDecodeThreads = 192;
-constexpr uint32_t kTileABytes = 128 * 128;  // 128 rows x 64 bf16
 
 struct DecodeSmemTail {
   uint64_t full[kMaxStages];
@@ -51,15 +54,18 @@ struct DecodeSmemTail {
 };
 
 // Pipeline buffers; after the main loop they hold the parked partial.
+template <int TM>
 __host__ __device__ inline size_t decode_pipe_bytes(int stages, int n_pad, int kc) {
-  size_t pipe = (size_t)stages * kc * (kTileABytes + (size_t)n_pad * 128);
-  if (pipe < park_area_bytes(n_pad)) pipe = park_area_bytes(n_pad);
+  size_t pipe = (size_t)stages * kc * (TileShape<TM>::kSliceBytes + (size_t)n_pad * 128);
+  const size_t park = park_area_bytes(n_pad, TileShape<TM>::kParkStride);
+  if (pipe < park) pipe = park;
   return (pipe + 127) & ~size_t(127);
 }
 
-__device__ __forceinline__ void add_f4x4(float* y, const float4* a) {
+template <int N>
+__device__ __forceinline__ void add_f4(float* y, const float4* a) {
 #pragma unroll
-  for (int k4 = 0; k4 < 4; ++k4) {
+  for (int k4 = 0; k4 < N / 4; ++k4) {
     y[4 * k4 + 0] += a[k4].x;
     y[4 * k4 + 1] += a[k4].y;
     y[4 * k4 + 2] += a[k4].z;
@@ -72,31 +78,44 @@ __device__ __forceinline__ void decode_fail(const PagedParams& p, DecodeSmemTail
   tl->abort = 1;
 }
 
+// Head row of local tile row i.  M = 128: i.  M = 64, half h: rows 0-31 are
+// head rows 32h .. 32h+31, rows 32-63 are 64 + 32h .. 64 + 32h + 31.
+template <int TM>
+__device__ __forceinline__ int head_row(int i, int half) {
+  if (TM == 128) return i;
+  return i < 32 ? 32 * half + i : 64 + 32 * half + (i - 32);
+}
+
+template <int TM>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     qkv_rope_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                            const PagedParams p) {
+  using TS = TileShape<TM>;
+  constexpr int RG = TS::kRowsPerThread;  // rows per finishing thread
+  constexpr int YS = TS::kParkStride;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.stages;
   const int KC = p.kc;
   const int n_pad = p.n_pad;
   const uint32_t b_chunk = (uint32_t)n_pad * 128u;
-  const uint32_t a_stage = (uint32_t)KC * kTileABytes;
+  const uint32_t a_stage = (uint32_t)KC * TS::kSliceBytes;
   const uint32_t b_stage = (uint32_t)KC * b_chunk;
   const uint32_t stage_bytes = a_stage + b_stage;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + (size_t)S * a_stage;
-  const size_t pipe_bytes = decode_pipe_bytes(S, n_pad, KC);
-  uint8_t* recv_smem = smem + pipe_bytes;
-  DecodeSmemTail* tl = reinterpret_cast<DecodeSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits));
+  uint8_t* recv_smem = smem + decode_pipe_bytes<TM>(S, n_pad, KC);
+  DecodeSmemTail* tl =
+      reinterpret_cast<DecodeSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits, TS::kChunkBytes));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
+  const int head = TM == 128 ? tile : tile >> 1;
+  const int half = TM == 128 ? 0 : tile & 1;
   const int num_kc = p.d_model / (kBK * KC);
   const int kc0 = (int)((long long)split * num_kc / p.splits);
   const int kc1 = (int)((long long)(split + 1) * num_kc / p.splits);
   const int nk = kc1 - kc0;  // pipeline stages (KC chunks each) of this CTA
-  const int row0 = tile * kHeadDim;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -109,7 +128,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     fence_mbar_init();
     // the partials this CTA will receive: (splits - 1) per owned chunk
     mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
-                                         kChunkBytes);
+                                         TS::kChunkBytes);
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
@@ -128,19 +147,26 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   volatile int* abort_flag = &tl->abort;
   // Epilogue warps: RoPE values of the first finished token and the bias of
   // the thread's row groups, fetched before the main loop ends.
-  float4 cs0[4], sn0[4];
-  float bias_y[16], bias_p[16];
+  float4 cs0[RG / 4], sn0[RG / 4];
+  float bias_y[RG], bias_p[RG];
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_w = make_l2_policy_evict_first();  // weights are streamed once
-      const uint64_t pol_x = make_l2_policy_evict_last();   // x_hat is re-read by every head
+      const uint64_t pol_x = make_l2_policy_evict_last();   // x_hat is re-read by every tile
+      auto load_w = [&](int s, int i) {
+        if (TM == 128)
+          tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, tile * 128, (kc0 + i) * KC, pol_w);
+        else
+          tma_load_5d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, 0, 0, 4 * head + half,
+                      (kc0 + i) * KC, pol_w);
+      };
       // W tiles of the first stages do not depend on the prep kernel.
       const int pre = nk < S ? nk : S;
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
-        tma_load_3d(a_smem + (size_t)i * a_stage, &tmap_w, &tl->full[i], 0, row0, (kc0 + i) * KC, pol_w);
+        load_w(i, i);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i)
@@ -153,14 +179,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&tl->full[s], stage_bytes);
-        tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, row0, (kc0 + i) * KC, pol_w);
+        load_w(s, i);
         tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (kc0 + i) * KC, pol_x);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ UMMA issue
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(128, n_pad);
+      const uint32_t idesc = umma_idesc_bf16(TM, n_pad);
       for (int i = 0; i < nk; ++i) {
         const int s = i % S;
         const uint32_t ph = (uint32_t)(i / S) & 1u;
@@ -170,7 +196,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         }
         tc_fence_after();
         for (int kc = 0; kc < KC; ++kc) {
-          const uint64_t ad = umma_desc_sw128(smem_u32(a_smem + (size_t)s * a_stage + (size_t)kc * kTileABytes));
+          const uint64_t ad =
+              umma_desc_sw128(smem_u32(a_smem + (size_t)s * a_stage + (size_t)kc * TS::kSliceBytes));
           const uint64_t bd = umma_desc_sw128(smem_u32(b_smem + (size_t)s * b_stage + (size_t)kc * b_chunk));
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
@@ -181,27 +208,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       umma_commit(&tl->accum);
     }
   } else {
-    // ------------------------------------------------ epilogue, phase A (warps 2-5)
-    // Park this CTA's partial accumulator, token-major, in its own smem.
+    // ------------------------------------------------ epilogue (warps 2-5)
     const int ept = threadIdx.x - 64;  // 0..127
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;  // accumulator row = TMEM lane
+    // accumulator row held by this lane (M = 64: lanes 16-31 of each quarter hold none)
+    const int r = TM == 128 ? q4 * 32 + lane : (lane < 16 ? q4 * 16 + lane : -1);
     const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16);
     const int T = p.num_tokens;
+    // Finishing thread (j, g): token c*16 + j of chunk c, tile rows RG*g .. +RG-1
+    // (8 consecutive lanes: 8 tokens of one row group, no bank conflicts);
+    // partner rows RG*(g ^ 4) hold the rotate-half partners.
+    const int j = ept & 15, g = ept >> 4, gp = g ^ 4;
+    const int hr0 = head_row<TM>(RG * g, half), hrp0 = head_row<TM>(RG * gp, half);
+    const float sign = g < 4 ? -1.f : 1.f;
+    const bool rot = head < p.n_heads + p.n_kv_heads;
+    const int rank = split;  // cluster (1, splits, 1): rank == blockIdx.y
+    const int nranks = p.splits;
     pdl_wait();
     for (int t = ept; t < T; t += 128) {
       tl->pos[t] = p.tok_pos[t];
       tl->slot[t] = p.tok_slot[t];
     }
     {
-      // RoPE values of this thread's first phase-B token, fetched while the
-      // main loop runs (same (token, row group) mapping as phase B).
-      const int t0 = (int)cluster_ctarank() * 16 + (ept & 15);
-      if (t0 < T && tile < p.n_heads + p.n_kv_heads) load_rope16(p, p.tok_pos[t0], ept >> 4, cs0, sn0);
+      const int t0 = rank * 16 + j;
+      if (t0 < T && rot) load_rope_n<RG>(p, p.tok_pos[t0], hr0, cs0, sn0);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        bias_y[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * (ept >> 4) + i]) : 0.f;
-        bias_p[i] = p.bias ? __bfloat162float(p.bias[row0 + 16 * ((ept >> 4) ^ 4) + i]) : 0.f;
+      for (int i = 0; i < RG; ++i) {
+        bias_y[i] = p.bias ? __bfloat162float(p.bias[head * kHeadDim + hr0 + i]) : 0.f;
+        bias_p[i] = p.bias ? __bfloat162float(p.bias[head * kHeadDim + hrp0 + i]) : 0.f;
       }
     }
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
@@ -212,8 +246,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     // Park the partial token-major in the idle pipeline buffers, four 16-token
     // chunks at a time; a chunk finished by another rank is sent to it by
     // bulk copy as soon as its group is parked.
-    const int rank = split;  // cluster (1, splits, 1): rank == blockIdx.y
-    const int nranks = p.splits;
     float* part = reinterpret_cast<float*>(smem);
     const uint32_t part_u32 = smem_u32(part);
     const int n_chunks = n_pad / 16;
@@ -225,12 +257,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         for (int cc = 0; cc < 4; ++cc)
           if (cc < nc) tmem_ld16_nowait(taddr + (uint32_t)((c0 + cc) * 16), v[cc]);
         tmem_wait_ld();
+        if (r >= 0) {
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc)
-          if (cc < nc) {
+          for (int cc = 0; cc < 4; ++cc)
+            if (cc < nc) {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * kYStride + r] = __uint_as_float(v[cc][jj]);
-          }
+              for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * YS + r] = __uint_as_float(v[cc][jj]);
+            }
+        }
       }
       bool remote = false;
       for (int cc = 0; cc < nc; ++cc) remote |= (c0 + cc) % nranks != rank;
@@ -242,9 +276,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             const int c = c0 + cc, owner = c % nranks;
             if (owner == rank) continue;
             const int slot = recv_slot(c / nranks, nranks, owner, rank);
-            bulk_copy_to_cluster(map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * kChunkBytes, (uint32_t)owner),
-                                 part_u32 + (uint32_t)c * kChunkBytes, kChunkBytes,
-                                 map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)owner));
+            bulk_copy_to_cluster(
+                map_smem_to_rank(smem_u32(recv_smem) + (uint32_t)slot * TS::kChunkBytes, (uint32_t)owner),
+                part_u32 + (uint32_t)c * TS::kChunkBytes, TS::kChunkBytes,
+                map_smem_to_rank(smem_u32(&tl->recv), (uint32_t)owner));
           }
         }
       }
@@ -253,10 +288,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     named_bar_sync(1, 128);  // the owned chunks are parked
 
     // ------------------------------------------------ finish the owned chunks
-    // thread (j, g8) owns token c*16 + j and rows 16*g8 .. +15 of chunk c.
-    const int j = ept & 15, g8 = ept >> 4;  // 8 consecutive lanes: 8 tokens, one row group (no bank conflicts)
-    const bool rot = tile < p.n_heads + p.n_kv_heads;
-    const int gp = g8 ^ 4;
     const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
     if (!got && lane == 0) decode_fail(p, tl, kStatusTimeoutCluster);
     if (got && *abort_flag == 0) {
@@ -265,21 +296,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         const int t = c * 16 + j;
         if (t >= T) continue;
         const int pos = tl->pos[t];
-        float4 cs[4], sn[4];
+        float4 cs[RG / 4], sn[RG / 4];
         if (rot) {
           if (c == rank) {
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
+            for (int k4 = 0; k4 < RG / 4; ++k4) {
               cs[k4] = cs0[k4];
               sn[k4] = sn0[k4];
             }
           } else {
-            load_rope16(p, pos, g8, cs, sn);
+            load_rope_n<RG>(p, pos, hr0, cs, sn);
           }
         }
-        float y[16], yp[16];
+        float y[RG], yp[RG];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < RG; ++i) {
           y[i] = bias_y[i];
           yp[i] = bias_p[i];
         }
@@ -287,28 +318,28 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         // loads issued before the first add
         const int oc = c / nranks;
         for (int q0 = 0; q0 < nranks; q0 += 2) {
-          float4 a[2][4], b[2][4];
+          float4 a[2][RG / 4], b[2][RG / 4];
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             const int q = q0 + qq < nranks ? q0 + qq : q0;
-            const float* src = q == rank ? part + t * kYStride
-                                         : recv + (size_t)recv_slot(oc, nranks, rank, q) * (kChunkBytes / 4) +
-                                               (size_t)j * kYStride;
+            const float* src = q == rank ? part + t * YS
+                                         : recv + (size_t)recv_slot(oc, nranks, rank, q) * (TS::kChunkBytes / 4) +
+                                               (size_t)j * YS;
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) a[qq][k4] = reinterpret_cast<const float4*>(src + 16 * g8)[k4];
+            for (int k4 = 0; k4 < RG / 4; ++k4) a[qq][k4] = reinterpret_cast<const float4*>(src + RG * g)[k4];
             if (rot) {
 #pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4) b[qq][k4] = reinterpret_cast<const float4*>(src + 16 * gp)[k4];
+              for (int k4 = 0; k4 < RG / 4; ++k4) b[qq][k4] = reinterpret_cast<const float4*>(src + RG * gp)[k4];
             }
           }
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             if (q0 + qq >= nranks) break;
-            add_f4x4(y, a[qq]);
-            if (rot) add_f4x4(yp, b[qq]);
+            add_f4<RG>(y, a[qq]);
+            if (rot) add_f4<RG>(yp, b[qq]);
           }
         }
-        store_rows16(p, tile, t, g8, pos, tl->slot[t], y, yp, cs, sn);
+        store_rows_n<RG>(p, head, t, hr0, sign, pos, tl->slot[t], y, yp, cs, sn);
       }
     }
     if (ept == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
@@ -323,14 +354,23 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   }
 }
 
-size_t decode_smem_bytes(int stages, int n_pad, int kc, int splits) {
-  return 1024 + decode_pipe_bytes(stages, n_pad, kc) + recv_area_bytes(n_pad, splits) + sizeof(DecodeSmemTail);
+template <int TM>
+size_t decode_smem_bytes_t(int stages, int n_pad, int kc, int splits) {
+  return 1024 + decode_pipe_bytes<TM>(stages, n_pad, kc) +
+         recv_area_bytes(n_pad, splits, TileShape<TM>::kChunkBytes) + sizeof(DecodeSmemTail);
 }
 
-cudaError_t launch_qkv_rope_decode(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
+size_t decode_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits) {
+  return tile_m == 64 ? decode_smem_bytes_t<64>(stages, n_pad, kc, splits)
+                      : decode_smem_bytes_t<128>(stages, n_pad, kc, splits);
+}
+
+template <int TM>
+static cudaError_t launch_decode_t(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                    int tiles, cudaStream_t stream) {
-  const size_t smem = decode_smem_bytes(p.stages, p.n_pad, p.kc, p.splits);
-  cudaError_t e = cudaFuncSetAttribute(qkv_rope_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = decode_smem_bytes_t<TM>(p.stages, p.n_pad, p.kc, p.splits);
+  cudaError_t e =
+      cudaFuncSetAttribute(qkv_rope_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, p.splits, 1);
@@ -346,13 +386,20 @@ cudaError_t launch_qkv_rope_decode(const CUtensorMap& tmap_w, const CUtensorMap&
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, qkv_rope_decode_kernel, tmap_w, tmap_x, p);
+  return cudaLaunchKernelEx(&cfg, qkv_rope_decode_kernel<TM>, tmap_w, tmap_x, p);
+}
+
+cudaError_t launch_qkv_rope_decode(int tile_m, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                                   const PagedParams& p, int tiles, cudaStream_t stream) {
+  return tile_m == 64 ? launch_decode_t<64>(tmap_w, tmap_x, p, tiles, stream)
+                      : launch_decode_t<128>(tmap_w, tmap_x, p, tiles, stream);
 }
 
 // Largest cluster count that can be resident at once for a given split.
-int decode_max_active_clusters(int splits, int n_pad, int stages, int kc) {
-  const size_t smem = decode_smem_bytes(stages, n_pad, kc, splits);
-  if (cudaFuncSetAttribute(qkv_rope_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+template <int TM>
+static int decode_max_active_clusters_t(int splits, int n_pad, int stages, int kc) {
+  const size_t smem = decode_smem_bytes_t<TM>(stages, n_pad, kc, splits);
+  if (cudaFuncSetAttribute(qkv_rope_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return 0;
   cudaLaunchConfig_t cfg = {};
@@ -367,11 +414,16 @@ int decode_max_active_clusters(int splits, int n_pad, int stages, int kc) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, qkv_rope_decode_kernel, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, qkv_rope_decode_kernel<TM>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return n;
+}
+
+int decode_max_active_clusters(int tile_m, int splits, int n_pad, int stages, int kc) {
+  return tile_m == 64 ? decode_max_active_clusters_t<64>(splits, n_pad, stages, kc)
+                      : decode_max_active_clusters_t<128>(splits, n_pad, stages, kc);
 }
 
 }  // namespace krt

@@ -79,41 +79,71 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// cos/sin values of rows 16*g8 .. +15 at position `pos` (16-byte loads),
-// issued ahead of their use so the gather latency overlaps other work.
-__device__ __forceinline__ void load_rope16(const PagedParams& p, int pos, int g8, float4* cs, float4* sn) {
+// Row stride (floats) of the token-major staging buffers: 128 rows + 4 pad.
+constexpr int kYStride = 132;
+
+// Split-K exchange inside a cluster.  Each CTA parks its fp32 partial tile
+// token-major ([n_pad][rows + 4]); the 16-token chunk c is finished by
+// cluster rank c % splits, which receives the other ranks' partials of that
+// chunk by bulk copy into its receive area:
+//   slot(oc, q) = oc * (splits - 1) + (q < owner ? q : q - 1)
+// for its oc-th owned chunk and source rank q.
+//
+// A tile is 128 weight rows (UMMA M = 128) or 64 (M = 64, where the
+// accumulator row i sits in TMEM lane 32 * (i / 16) + i % 16).
+template <int TM>
+struct TileShape {
+  static constexpr int kRows = TM;
+  static constexpr int kParkStride = TM + 4;                 // floats per parked token row
+  static constexpr uint32_t kChunkBytes = 16u * (TM + 4) * 4u;  // one 16-token chunk of a partial
+  static constexpr int kRowsPerThread = TM / 8;               // finishing thread: 8 row groups x 16 tokens
+  static constexpr uint32_t kSliceBytes = TM * 128u;          // one 64-column slice of the weight tile
+};
+constexpr uint32_t kChunkBytes = TileShape<128>::kChunkBytes;
+__host__ __device__ inline int owned_chunks(int n_chunks, int splits, int rank) {
+  return rank < n_chunks ? (n_chunks - 1 - rank) / splits + 1 : 0;
+}
+__host__ __device__ inline size_t recv_area_bytes(int n_pad, int splits, uint32_t chunk_bytes = kChunkBytes) {
+  return splits > 1 ? (size_t)owned_chunks(n_pad / 16, splits, 0) * (splits - 1) * chunk_bytes : 0;
+}
+__host__ __device__ inline size_t park_area_bytes(int n_pad, int park_stride = kYStride) {
+  return (size_t)n_pad * park_stride * sizeof(float);
+}
+__host__ __device__ inline int recv_slot(int oc, int splits, int owner, int q) {
+  return oc * (splits - 1) + (q < owner ? q : q - 1);
+}
+
+// N (8 or 16) RoPE table values at `pos`, head rows r0 .. r0 + N - 1.
+template <int N>
+__device__ __forceinline__ void load_rope_n(const PagedParams& p, int pos, int r0, float4* cs, float4* sn) {
   if (pos < 0) pos = 0;
-  const float4* c4 = reinterpret_cast<const float4*>(p.cos + (size_t)pos * kHeadDim + 16 * g8);
-  const float4* s4 = reinterpret_cast<const float4*>(p.sin + (size_t)pos * kHeadDim + 16 * g8);
+  const float4* c4 = reinterpret_cast<const float4*>(p.cos + (size_t)pos * kHeadDim + r0);
+  const float4* s4 = reinterpret_cast<const float4*>(p.sin + (size_t)pos * kHeadDim + r0);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < N / 4; ++q) {
     cs[q] = __ldg(c4 + q);
     sn[q] = __ldg(s4 + q);
   }
 }
 
-// Epilogue, phase B: thread (token t, row group g8) of a head tile writes
-// rows row0 + 16*g8 .. +15 of token t.
-//   y[i]  = qkv[t][row0 + 16*g8 + i] (fp32, bias included)
-//   yp[i] = the rotate-half partner rows 16*(g8^4) + i (Q/K tiles only)
-//   Q/K tiles: out = y*cos + rotate_half(y)*sin with rotate_half = [-y2, y1]
-//              per head (fusion_forge.py:92-139); cs/sn from load_rope16;
-//   V tiles:   out = y, unrotated (fusion_forge.py:161-162).
-// Q goes to q[t][tile*128 + ...]; K/V to pool slot `slot` and, when given, to
-// the dense k/v outputs.  Two 16-byte stores per destination.
-__device__ __forceinline__ void store_rows16(const PagedParams& p, int tile, int t, int g8, int pos, long long slot,
-                                             const float* y, const float* yp, const float4* cs, const float4* sn) {
+// N (8 or 16) consecutive head rows r0 .. r0 + N - 1 of token t in head
+// `head` (Q heads, then K, then V): y = the rows, yp = their rotate-half
+// partner rows (r0 ^ 64 ..), sign = -1 for the first half of the head.  Q/K
+// rows are rotated, V rows are not; Q goes to q[t], K/V to the pool slot and,
+// when given, the dense k/v outputs, with 16-byte stores.
+template <int N>
+__device__ __forceinline__ void store_rows_n(const PagedParams& p, int head, int t, int r0, float sign, int pos,
+                                             long long slot, const float* y, const float* yp, const float4* cs,
+                                             const float4* sn) {
   const int Hq = p.n_heads, Hkv = p.n_kv_heads;
-  const bool is_q = tile < Hq;
-  const bool is_v = tile >= Hq + Hkv;
-  const int g = is_q ? tile : (is_v ? tile - Hq - Hkv : tile - Hq);
-  const int r0 = 16 * g8;
-  float out[16];
+  const bool is_q = head < Hq;
+  const bool is_v = head >= Hq + Hkv;
+  const int g = is_q ? head : (is_v ? head - Hq - Hkv : head - Hq);
+  float out[N];
   if (!is_v) {
     if (pos < 0) return;
-    const float sign = g8 < 4 ? -1.f : 1.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < N / 4; ++q) {
       out[4 * q + 0] = y[4 * q + 0] * cs[q].x + sign * yp[4 * q + 0] * sn[q].x;
       out[4 * q + 1] = y[4 * q + 1] * cs[q].y + sign * yp[4 * q + 1] * sn[q].y;
       out[4 * q + 2] = y[4 * q + 2] * cs[q].z + sign * yp[4 * q + 2] * sn[q].z;
@@ -121,57 +151,32 @@ __device__ __forceinline__ void store_rows16(const PagedParams& p, int tile, int
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) out[i] = y[i];
+    for (int i = 0; i < N; ++i) out[i] = y[i];
   }
-  uint4 v0, v1;
-  v0.x = pack_bf16x2(out[0], out[1]);
-  v0.y = pack_bf16x2(out[2], out[3]);
-  v0.z = pack_bf16x2(out[4], out[5]);
-  v0.w = pack_bf16x2(out[6], out[7]);
-  v1.x = pack_bf16x2(out[8], out[9]);
-  v1.y = pack_bf16x2(out[10], out[11]);
-  v1.z = pack_bf16x2(out[12], out[13]);
-  v1.w = pack_bf16x2(out[14], out[15]);
+  uint4 v[N / 8];
+#pragma unroll
+  for (int h = 0; h < N / 8; ++h)
+    v[h] = make_uint4(pack_bf16x2(out[8 * h + 0], out[8 * h + 1]), pack_bf16x2(out[8 * h + 2], out[8 * h + 3]),
+                      pack_bf16x2(out[8 * h + 4], out[8 * h + 5]), pack_bf16x2(out[8 * h + 6], out[8 * h + 7]));
   if (is_q) {
-    uint4* dst = reinterpret_cast<uint4*>(p.q + (size_t)t * p.q_stride + (size_t)tile * kHeadDim + r0);
-    dst[0] = v0;
-    dst[1] = v1;
+    uint4* dst = reinterpret_cast<uint4*>(p.q + (size_t)t * p.q_stride + (size_t)head * kHeadDim + r0);
+#pragma unroll
+    for (int h = 0; h < N / 8; ++h) dst[h] = v[h];
     return;
   }
   const size_t tok_elems = (size_t)2 * Hkv * kHeadDim;
   const size_t head_off = (size_t)(is_v ? Hkv + g : g) * kHeadDim + r0;
   if (slot >= 0) {
     uint4* dst = reinterpret_cast<uint4*>(p.pool + (size_t)slot * tok_elems + head_off);
-    dst[0] = v0;
-    dst[1] = v1;
+#pragma unroll
+    for (int h = 0; h < N / 8; ++h) dst[h] = v[h];
   }
   __nv_bfloat16* dense = is_v ? p.v : p.k;
   if (dense) {
     uint4* dst = reinterpret_cast<uint4*>(dense + ((size_t)t * Hkv + g) * kHeadDim + r0);
-    dst[0] = v0;
-    dst[1] = v1;
+#pragma unroll
+    for (int h = 0; h < N / 8; ++h) dst[h] = v[h];
   }
-}
-
-// Row stride (floats) of the token-major staging buffers: 128 rows + 4 pad.
-constexpr int kYStride = 132;
-
-// Split-K exchange inside a cluster.  Each CTA parks its fp32 partial tile
-// token-major ([n_pad][kYStride]); the 16-token chunk c is finished by
-// cluster rank c % splits, which receives the other ranks' partials of that
-// chunk by bulk copy into its receive area:
-//   slot(oc, q) = oc * (splits - 1) + (q < owner ? q : q - 1)
-// for its oc-th owned chunk and source rank q.
-constexpr uint32_t kChunkBytes = 16u * kYStride * 4u;  // one chunk of a partial
-__host__ __device__ inline int owned_chunks(int n_chunks, int splits, int rank) {
-  return rank < n_chunks ? (n_chunks - 1 - rank) / splits + 1 : 0;
-}
-__host__ __device__ inline size_t recv_area_bytes(int n_pad, int splits) {
-  return splits > 1 ? (size_t)owned_chunks(n_pad / 16, splits, 0) * (splits - 1) * kChunkBytes : 0;
-}
-__host__ __device__ inline size_t park_area_bytes(int n_pad) { return (size_t)n_pad * kYStride * sizeof(float); }
-__host__ __device__ inline int recv_slot(int oc, int splits, int owner, int q) {
-  return oc * (splits - 1) + (q < owner ? q : q - 1);
 }
 
 __device__ __forceinline__ void ld_smem_16f(const float* src, float* dst) {

@@ -21,7 +21,7 @@
 // lane adds the bias and parks row r token-major in its group's buffer;
 // (B) thread (token j, rows 16*g8..+15) applies RoPE with the partner rows
 // r ^ 64 and writes 16-byte vectors to Q or to the paged pool
-// (store_rows16).  cos/sin gathers are issued before the TMEM load so their
+// (store_rows_n).  cos/sin gathers are issued before the TMEM load so their
 // latency overlaps it; per-token positions and slots are staged in shared
 // memory once per tile.
 //
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const int jt = c0 + j;
         const int pos = tl->pos[jt];
         float4 cs[4], sn[4];
-        if (rot) load_rope16(p, pos, g8, cs, sn);
+        if (rot) load_rope_n<16>(p, pos, 16 * g8, cs, sn);
         float acc[16];
         tmem_ld16(taddr + (uint32_t)c0, acc);
 #pragma unroll
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           float y[16], yp[16];
           ld_smem_16f(ybuf + j * kYStride + 16 * g8, y);
           ld_smem_16f(ybuf + j * kYStride + 16 * (g8 ^ 4), yp);
-          store_rows16(p, head, t_base + jt, g8, pos, tl->slot[jt], y, yp, cs, sn);
+          store_rows_n<16>(p, head, t_base + jt, 16 * g8, g8 < 4 ? -1.f : 1.f, pos, tl->slot[jt], y, yp, cs, sn);
         }
         named_bar_sync(bar_grp, 128);
       }

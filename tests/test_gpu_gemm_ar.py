@@ -57,6 +57,14 @@ def test_gemm_single_gpu(torch_cuda, T, K, N):
     np.testing.assert_allclose(y.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("T,K,N", [(33, 1536, 384), (200, 640, 256)])
+def test_gemm_half_height_tiles(torch_cuda, monkeypatch, T, K, N):
+    """KRT_GEMM_TILE_M=64 selects 64-row weight tiles (read when a shape is
+    first configured; these shapes are used nowhere else in the suite)."""
+    monkeypatch.setenv("KRT_GEMM_TILE_M", "64")
+    test_gemm_single_gpu(torch_cuda, T, K, N)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

@@ -113,7 +113,8 @@ def test_paged_gqa_golden(torch_cuda, krt, kind):
 @pytest.mark.parametrize("kind,num_seqs,tokens_per_seq,ctx", [
     ("decode", 64, 1, 2048),      # Llama-3-8B decode batch 64 at context 2048
     ("decode", 5, 1, 77),         # ragged small batch
-    ("decode", 128, 1, 300),      # decode batch 128
+    ("decode", 128, 1, 300),      # decode batch 128 (half-head tiles)
+    ("decode", 200, 1, 90),       # decode batch 200 (whole-head tiles)
     ("prefill", 1, 300, None),    # one sequence, two token blocks, ragged tail
     ("prefill", 3, 100, None),    # three sequences
 ])
