@@ -37,6 +37,7 @@ METRIC = "decode tokens/s per box at TP=1/2/4/8; fused QKV+RoPE & GEMM+AR % roof
 HIDDEN, N_HEADS, N_KV, HEAD_DIM, INTER = 4096, 32, 8, 128, 14336
 BATCH, CTX, BLOCK = 64, 2048, 16
 L2_BYTES = 126 * 1024 * 1024
+NVLINK_GBS = 770.0  # measured B200 peer-copy bandwidth per direction over NVLink 5 (900 GB/s nominal)
 
 
 def peaks():
@@ -188,14 +189,32 @@ class Rig:
         self.comm_handle = comm.handle if comm is not None else None
         self.launches_per_step = 4  # prep + decode, o_proj, down_proj
 
-    def step(self, i, parts=(0, 1, 2)):
-        qa, oa, da = self.args[i % self.n_layers]
+    def step(self, i, parts=(0, 1, 2), args=None):
+        qa, oa, da = (args or self.args)[i % self.n_layers]
         if 0 in parts:
             self.lib.qkv_rope_decode(qa)
         if 1 in parts:
             self.lib.rowparallel_gemm_ar(self.comm_handle, oa)
         if 2 in parts:
             self.lib.rowparallel_gemm_ar(self.comm_handle, da)
+
+    def io_set(self):
+        """A second set of step inputs and outputs (and the per-layer call
+        arguments that use them), for pipelining host copies across steps."""
+        torch, _lib = self.torch, self.lib
+        io = {k: torch.empty_like(getattr(self, k)) for k in ("x", "attn", "act", "q", "y_o", "y_d")}
+        for k in ("x", "attn", "act"):
+            io[k].copy_(getattr(self, k))
+        io["ws_qkv"] = torch.zeros_like(self.ws_qkv)
+        io["args"] = []
+        for L in self.layers:
+            qa = _lib.paged_args(io["x"], L.w_qkv, None, L.gamma, self.cos, self.sin, self.positions, self.token_seq,
+                                 self.block_table, self.pool, io["q"], self.hq, self.hkv, self.num_blocks, BLOCK,
+                                 io["ws_qkv"])
+            oa = _lib.gemm_ar_args(io["attn"], L.w_o, io["y_o"], self.ws_gemm)
+            da = _lib.gemm_ar_args(io["act"], L.w_d, io["y_d"], self.ws_gemm)
+            io["args"].append((qa, oa, da))
+        return io
 
     def graphs(self, parts=(0, 1, 2), per_graph=1):
         """One CUDA graph per starting layer; graph k holds steps
@@ -313,37 +332,98 @@ def run_krt(args, rank, world, local_rank):
             g[0][i % len(g[0])].replay()
         kms = max_over_ranks(torch, timed_graph_replays(torch, g, reps, world), world) / reps
         ach = nbytes / (kms * 1e-3) / 1e9
-        kernels.append({"kernel": name, "bound": "hbm", "us": round(kms * 1e3, 3), "algorithmic_bytes": nbytes,
-                        "bytes": what, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                        "frac": round(ach / hbm, 4), "traffic": traffic.get(f"{name}_tp{world}")})
+        entry = {"kernel": name, "bound": "hbm", "us": round(kms * 1e3, 3), "algorithmic_bytes": nbytes,
+                 "bytes": what, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                 "frac": round(ach / hbm, 4), "traffic": traffic.get(f"{name}_tp{world}")}
+        if part > 0 and world > 1:
+            # fused allreduce of the [64, 4096] output: bus bytes as NCCL counts
+            # them (2 (w-1)/w x bf16 message) and the bytes this build puts on
+            # NVLink per GPU (4 B per value in each of the two phases)
+            msg = BATCH * HIDDEN * 2
+            bus = 2 * (world - 1) / world * msg
+            wire = 2 * (world - 1) / world * BATCH * HIDDEN * 4
+            target_us = max(nbytes / hbm / 1e3, wire / NVLINK_GBS / 1e3)
+            entry.update({"allreduce_bus_bytes": int(bus), "allreduce_bus_GBps": round(bus / (kms * 1e-3) / 1e9, 1),
+                          "nvlink_wire_bytes_per_gpu": int(wire), "nvlink_peak_GBps": NVLINK_GBS,
+                          "roofline_us": round(target_us, 3), "frac_of_roofline": round(target_us / (kms * 1e3), 4)})
+        kernels.append(entry)
     rig.check_status()
     dominant = max(kernels, key=lambda k: k["us"])
 
-    # end to end through the C ABI with host buffers: H2D of the step's
-    # activations, the three calls, D2H of q and both layer outputs
+    # End to end through the C ABI with host buffers: every step copies its
+    # activations from pinned host memory, runs the three calls and copies q
+    # and both layer outputs back.  Two input/output sets alternate so that a
+    # step's copies overlap its neighbours' kernels (H2D and D2H on their own
+    # streams); 8 steps per CUDA graph.
+    ios = [rig.io_set(), rig.io_set()]
     pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())
-    hx, hattn, hact = pin(rig.x), pin(rig.attn), pin(rig.act)
-    hq_out, hyo, hyd = (torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (rig.q, rig.y_o, rig.y_d))
-    h2d = sum(t.numel() * t.element_size() for t in (hx, hattn, hact))
-    d2h = sum(t.numel() * t.element_size() for t in (hq_out, hyo, hyd))
-    e2e_steps = max(4, min(args.steps, 50))
-    for i in range(2):
-        rig.step(i)
+    h_in = [{k: pin(io[k]) for k in ("x", "attn", "act")} for io in ios]
+    h_out = [{k: torch.empty(io[k].shape, dtype=io[k].dtype, pin_memory=True) for k in ("q", "y_o", "y_d")}
+             for io in ios]
+    h2d = sum(t.numel() * t.element_size() for t in h_in[0].values())
+    d2h = sum(t.numel() * t.element_size() for t in h_out[0].values())
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def e2e_steps_captured(first):
+        comp = torch.cuda.current_stream()
+        ev = lambda: torch.cuda.Event()
+        done_in, done_comp, done_out = {}, {}, {}
+        fork = ev()
+        fork.record(comp)
+        s_in.wait_event(fork)
+        s_out.wait_event(fork)
+        for i in range(first, first + STEPS_PER_GRAPH):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                if i - 2 in done_comp:
+                    s_in.wait_event(done_comp[i - 2])
+                for k in ("x", "attn", "act"):
+                    ios[b][k].copy_(h_in[b][k], non_blocking=True)
+                done_in[i] = ev()
+                done_in[i].record(s_in)
+            comp.wait_event(done_in[i])
+            if i - 2 in done_out:
+                comp.wait_event(done_out[i - 2])
+            rig.step(i, args=ios[b]["args"])
+            done_comp[i] = ev()
+            done_comp[i].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done_comp[i])
+                for k in ("q", "y_o", "y_d"):
+                    h_out[b][k].copy_(ios[b][k], non_blocking=True)
+                done_out[i] = ev()
+                done_out[i].record(s_out)
+        comp.wait_stream(s_in)
+        comp.wait_stream(s_out)
+
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        e2e_steps_captured(0)  # eager warm-up of the same sequence
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+    e2e_graphs = []
+    for k in range(rig.n_layers):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            e2e_steps_captured(k * STEPS_PER_GRAPH)
+        e2e_graphs.append(g)
+    e2e_steps = STEPS_PER_GRAPH * max(4, min(args.steps, 800) // STEPS_PER_GRAPH)
+    for g in e2e_graphs:
+        g.replay()
     barrier(torch, world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(e2e_steps):
-        rig.x.copy_(hx, non_blocking=True)
-        rig.attn.copy_(hattn, non_blocking=True)
-        rig.act.copy_(hact, non_blocking=True)
-        rig.step(i)
-        hq_out.copy_(rig.q, non_blocking=True)
-        hyo.copy_(rig.y_o, non_blocking=True)
-        hyd.copy_(rig.y_d, non_blocking=True)
+    for i in range(e2e_steps // STEPS_PER_GRAPH):
+        e2e_graphs[i % len(e2e_graphs)].replay()
     b.record()
     barrier(torch, world)
     e2e_ms = max_over_ranks(torch, a.elapsed_time(b), world) / e2e_steps
     rig.check_status()
+    for io in ios:
+        rc, bits = rig.lib.read_status(io["ws_qkv"])
+        if rc != 0:
+            raise RuntimeError(f"kernel status {bits:#x}")
 
     base = cpu_baseline() if rank == 0 else None
     if rank == 0:
@@ -365,7 +445,7 @@ def run_krt(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
     if comm is not None:
         import torch.distributed as dist
-        del graphs
+        del graphs, e2e_graphs
         torch.cuda.synchronize()
         comm.close()
         dist.barrier()

@@ -248,7 +248,8 @@ int decode_stages(int tile_m, int n_pad, int kc, int splits) {
 int decode_kc(int tile_m, int num_kb, int n_pad, int splits) {
   int kc = env_int("KRT_DECODE_KC", 4);
   if (kc < 1) kc = 1;
-  while (kc > 1 && ((num_kb % kc) != 0 || decode_stages(tile_m, n_pad, kc, splits) < 2)) kc >>= 1;
+  while (kc > 1 && ((num_kb % kc) != 0 || num_kb / kc < splits || decode_stages(tile_m, n_pad, kc, splits) < 2))
+    kc >>= 1;
   return kc;
 }
 

@@ -287,12 +287,13 @@ int gemm_stages(int tile_m, int n_pad, int kc, int splits) {
   return 0;
 }
 
-// Box depth with the most weight bytes in flight.
+// Box depth with the most weight bytes in flight, leaving every split at
+// least one box of the K range.
 int gemm_kc(int tile_m, int num_kb, int n_pad, int splits) {
   int best = 1;
   size_t best_bytes = 0;
   for (int kc = 4; kc >= 1; kc >>= 1) {
-    if (num_kb % kc != 0) continue;
+    if (num_kb % kc != 0 || num_kb / kc < splits) continue;
     const size_t bytes = (size_t)gemm_stages(tile_m, n_pad, kc, splits) * kc * tile_m * 128;
     if (bytes > best_bytes) {
       best_bytes = bytes;
