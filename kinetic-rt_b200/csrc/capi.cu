@@ -236,9 +236,15 @@ int env_int(const char* name, int dflt) {
   return (v && *v) ? std::atoi(v) : dflt;
 }
 
+// Shared memory per CTA the stage count may use: 227 KB (one CTA per SM) by
+// default; KRT_SMEM_CAP_KB lowers it for tuning (at 113 KB two kernels' CTAs
+// can share an SM, but the shallower weight pipeline measured slower on
+// B200: a Llama-3-8B decode layer step of 66.6 us against 51.3 us).
+size_t smem_cap_bytes() { return (size_t)env_int("KRT_SMEM_CAP_KB", 227) * 1024; }
+
 int decode_stages(int tile_m, int n_pad, int kc, int splits) {
   for (int st = kMaxStages; st >= 1; --st)
-    if (decode_smem_bytes(tile_m, st, n_pad, kc, splits) <= 227 * 1024) return st;
+    if (decode_smem_bytes(tile_m, st, n_pad, kc, splits) <= smem_cap_bytes()) return st;
   return 0;
 }
 

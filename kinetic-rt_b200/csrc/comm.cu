@@ -276,14 +276,15 @@ extern "C" int krt_allreduce(krt_comm* c, const void* send, void* recv, size_t c
 // ------------------------------------------------------ fused GEMM + allreduce
 namespace {
 
-int env_tile_m(const char* name, int dflt) {
+int env_int_value(const char* name, int dflt) {
   const char* v = std::getenv(name);
   return (v && *v) ? std::atoi(v) : dflt;
 }
 
 int gemm_stages(int tile_m, int n_pad, int kc, int splits) {
+  const size_t cap = (size_t)env_int_value("KRT_SMEM_CAP_KB", 227) * 1024;
   for (int st = kMaxStages; st >= 1; --st)
-    if (gemm_ar_smem_bytes(tile_m, st, n_pad, kc, splits) <= 227 * 1024) return st;
+    if (gemm_ar_smem_bytes(tile_m, st, n_pad, kc, splits) <= cap) return st;
   return 0;
 }
 
@@ -322,7 +323,7 @@ GemmCfg gemm_config(int n_out, int num_kb, int n_pad) {
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  int tile_m = env_tile_m("KRT_GEMM_TILE_M", 128);
+  int tile_m = env_int_value("KRT_GEMM_TILE_M", 128);
   if (tile_m != 64) tile_m = 128;
   const int tiles = n_out / tile_m;
   GemmCfg cfg{tile_m, tiles, 1, 1, 1};
