@@ -36,10 +36,17 @@ struct CommLayout {
   // and pair), so a warp's store covers 512 contiguous bytes.  One set of
   // areas per tile height (index 0: 128 rows, 1: 64 rows), so the slots and
   // epochs of the two tilings never alias.
-  size_t ll_stage_off[2];   // [world (source)][owned tiles][kMaxChunks][rows/32 pairs][128 threads]
+  // Two ranks exchange one-shot (each rank sends its whole partial to the
+  // other and both reduce), so their stage holds every tile, twice: uses of
+  // a (tile, chunk) alternate between the two copies by epoch parity, since
+  // nothing tells a sender that its peer has finished reading the previous
+  // use (a rank runs at most one launch ahead of the other).  More ranks
+  // reduce-scatter, and a rank's stage holds only the tiles it owns.
+  size_t ll_stage_off[2];   // [world (source)][stage tiles][kMaxChunks][rows/32 pairs][128 threads]
   size_t ll_result_off[2];  // [tiles][kMaxChunks][rows/32 pairs][128 threads]
-  size_t epoch_off[2];      // u32 [tiles][kMaxChunks] uses of each (tile, chunk), in 1..65535
+  size_t epoch_off[2];      // u32 [tiles][kMaxChunks] uses of each (tile, chunk), cycling 1..65534
   int owned_tiles[2];       // ceil(tiles / world): tile t is reduced by rank t % world
+  int stage_tiles[2];       // tile slots per source: 2 x all tiles (world 2) or the owned ones
   size_t total;
 };
 
@@ -61,8 +68,9 @@ inline CommLayout comm_layout(int world, int max_n) {
     const int tiles = max_n / rows;
     const size_t slot = (size_t)rows * 64;  // bytes: rows/32 pairs x 128 threads x 16
     L.owned_tiles[v] = (tiles + world - 1) / world;
+    L.stage_tiles[v] = world == 2 ? 2 * tiles : L.owned_tiles[v];
     L.ll_stage_off[v] = off;
-    L.ll_result_off[v] = up(off + (size_t)world * L.owned_tiles[v] * kMaxChunks * slot);
+    L.ll_result_off[v] = up(off + (size_t)world * L.stage_tiles[v] * kMaxChunks * slot);
     L.epoch_off[v] = up(L.ll_result_off[v] + (size_t)tiles * kMaxChunks * slot);
     off = up(L.epoch_off[v] + (size_t)tiles * kMaxChunks * 4);
   }

@@ -16,9 +16,12 @@
 // RG*g .. +RG-1, RG = rows / 8) of chunk `ch` then owns RG fp32 values of
 // this rank's partial product.
 //
-// Allreduce part, fused into the epilogue (two-shot over NVLink, world > 1),
-// in flagged 8-byte words (epoch and payload in one store each), so that no
-// memory fence and no separate flag is on the path:
+// Allreduce part, fused into the epilogue (world > 1), in flagged 8-byte
+// words (epoch and payload in one store each), so that no memory fence and
+// no separate flag is on the path.  Two ranks exchange one-shot: each sends
+// its partial chunk to both stages (alternating between two copies by epoch
+// parity) and both reduce it in rank order (one NVLink hop, the same bytes
+// as two-shot).  More ranks run two-shot:
 //   1. reduce-scatter: the partial chunk (16 tokens x rows features, fp32
 //      rounded to 24-bit floats with a 15-bit mantissa) is stored into the
 //      owner rank's stage [src][tile / world][chunk] (owner = tile % world);
@@ -86,10 +89,12 @@ __device__ __forceinline__ void gemm_fail(const GemmArParams& p, GemmSmemTail* t
 // Slot of one chunk; the word pair i of finishing thread `ept` is at
 // slot + 2 * (i * 128 + ept).
 template <int TM>
-__device__ __forceinline__ uint64_t* ll_stage(const CommView& cv, int holder, int src, int tile, int ch) {
+__device__ __forceinline__ uint64_t* ll_stage(const CommView& cv, int holder, int src, int tile, int ch,
+                                              uint32_t epoch) {
   constexpr int v = TM == 64 ? 1 : 0;
+  const int st = cv.world == 2 ? (int)(epoch & 1u) * (cv.L.stage_tiles[v] / 2) + tile : tile / cv.world;
   return reinterpret_cast<uint64_t*>(cv.base[holder] + cv.L.ll_stage_off[v]) +
-         (((size_t)src * cv.L.owned_tiles[v] + tile / cv.world) * kMaxChunks + ch) * (TM / 32 * 128 * 2);
+         (((size_t)src * cv.L.stage_tiles[v] + st) * kMaxChunks + ch) * (TM / 32 * 128 * 2);
 }
 template <int TM>
 __device__ __forceinline__ uint64_t* ll_result(const CommView& cv, int holder, int tile, int ch) {
@@ -284,17 +289,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int owner = tile % world;
     const float* recv = reinterpret_cast<const float*>(recv_smem);
     pdl_wait();  // Y and the exchange buffers may still be in use by the previous kernel
-    // Epoch of each (tile, chunk) this CTA finishes: its use count in 1..65535,
-    // the same on every rank since every rank runs the same launches.  A slot
-    // of the exchange only ever holds this launch's words or the previous
-    // use's (epoch - 1), never a matching stale word.
+    // Epoch of each (tile, chunk) this CTA finishes: its use count, cycling
+    // through 1..65534 (so consecutive uses alternate in parity), the same on
+    // every rank since every rank runs the same launches.  A slot of the
+    // exchange only ever holds this launch's words or an earlier use's,
+    // never a matching stale word.
     if (world > 1) {
       if (ept == 0) {
         uint32_t* ctr = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.epoch_off[TM == 64 ? 1 : 0]) +
                         (size_t)tile * kMaxChunks;
         for (int ch = crank, oc = 0; ch * 16 < T; ch += p.splits, ++oc) {
           uint32_t e = __ldcg(ctr + ch) + 1u;
-          if (e > 65535u) e = 1u;
+          if (e > 65534u) e = 1u;
           ctr[ch] = e;
           tl->epoch[oc] = e;
         }
@@ -342,21 +348,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else {
         // flagged words of two 24-bit floats into the owner's stage (local
-        // when this rank owns the tile)
+        // when this rank owns the tile); with two ranks into both stages
         const uint32_t epoch = tl->epoch[ch / nranks];
-        uint64_t* dst = ll_stage<TM>(cv, owner, cv.rank, tile, ch) + 2 * ept;
+        uint64_t w[RG / 2];
 #pragma unroll
-        for (int i = 0; i < NP; ++i)
-          st_ll2(dst + 256 * i, f24_pair_word(y[4 * i], y[4 * i + 1], epoch),
-                 f24_pair_word(y[4 * i + 2], y[4 * i + 3], epoch));
+        for (int i = 0; i < RG / 2; ++i) w[i] = f24_pair_word(y[2 * i], y[2 * i + 1], epoch);
+        for (int d = 0; d < (world == 2 ? 2 : 1); ++d) {
+          uint64_t* dst = ll_stage<TM>(cv, world == 2 ? d : owner, cv.rank, tile, ch, epoch) + 2 * ept;
+#pragma unroll
+          for (int i = 0; i < NP; ++i) st_ll2(dst + 256 * i, w[2 * i], w[2 * i + 1]);
+        }
       }
     }
     if (world > 1) {
       const uint64_t t0 = globaltimer_ns();
       bool ok = true;
-      if (cv.rank == owner) {
-        // ---- phase 2 (owner): every rank's words of the chunk, reduced in rank
-        // order; the bf16 result goes to Y and, as flagged words, to every peer
+      if (world == 2 || cv.rank == owner) {
+        // ---- phase 2 (owner; both ranks when there are two): every rank's
+        // words of the chunk, reduced in rank order; the bf16 result goes to
+        // Y and, with more than two ranks, as flagged words to every peer
         for (int ch = crank; ch * 16 < T; ch += p.splits) {
           const int t = ch * 16 + j;
           float acc[RG];
@@ -367,7 +377,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint64_t u[RG / 2];
 #pragma unroll
             for (int i = 0; i < RG / 2; ++i) u[i] = 0u;
-            if (ok) ok = poll_words_batch<NP, 48>(ll_stage<TM>(cv, cv.rank, q, tile, ch) + 2 * ept, 256, epoch, t0, u);
+            if (ok)
+              ok = poll_words_batch<NP, 48>(ll_stage<TM>(cv, cv.rank, q, tile, ch, epoch) + 2 * ept, 256, epoch, t0, u);
 #pragma unroll
             for (int i = 0; i < RG / 2; ++i) {
               const float2 v = f24_pair_unpack(u[i]);
@@ -379,7 +390,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint32_t w[RG / 2];
 #pragma unroll
           for (int i = 0; i < RG / 2; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
-          for (int q = 0; q < world; ++q) {
+          for (int q = 0; q < world && world > 2; ++q) {
             if (q == cv.rank) continue;
             uint64_t* rd = ll_result<TM>(cv, q, tile, ch) + 2 * ept;
 #pragma unroll
