@@ -354,6 +354,10 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   p.kc = cfg.kc;
   p.stages = cfg.stages;
   p.splits = cfg.splits;
+  // L2 prefetch ahead of the ring for short K loops (at most 8 stages per
+  // CTA), where the ring alone cannot put enough weight bytes in flight
+  // early; long loops already keep HBM busy and only gain L2 pressure.
+  p.prefetch = env_int("KRT_L2_PREFETCH_STAGES", (num_kb / p.kc + p.splits - 1) / p.splits <= 8 ? 4 : 0);
   int cols = 32;
   while (cols < p.n_pad) cols <<= 1;
   p.tmem_cols = cols;

@@ -91,6 +91,7 @@ struct GemmArParams {
   int y_stride;
   int num_tokens, n_pad, n_out, k_local;
   int splits, stages, kc, tmem_cols;
+  int prefetch;  // weight stages requested into L2 ahead of the shared-memory ring
   int* status;
   CommView comm;
 };

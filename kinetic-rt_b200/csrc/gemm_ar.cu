@@ -179,6 +179,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
         tma_load_3d(a_smem + (size_t)i * a_stage, &tmap_w, &tl->full[i], 0, row0, (kc0 + i) * KC, pol_w);
       }
+      // the next p.prefetch weight stages are requested into L2 beyond the ring
+      for (int i = pre; i < nk && i < pre + p.prefetch; ++i) tma_prefetch_l2_3d(&tmap_w, 0, row0, (kc0 + i) * KC);
       pdl_wait();  // X may come from the previous kernel
       for (int i = 0; i < pre; ++i)
         tma_load_3d(b_smem + (size_t)i * b_stage, &tmap_x, &tl->full[i], 0, 0, (kc0 + i) * KC, pol_x);
@@ -192,6 +194,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_arrive_expect_tx(&tl->full[s], stage_bytes);
         tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, row0, (kc0 + i) * KC, pol_w);
         tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (kc0 + i) * KC, pol_x);
+        if (i + p.prefetch < nk) tma_prefetch_l2_3d(&tmap_w, 0, row0, (kc0 + i + p.prefetch) * KC);
       }
     }
   } else if (warp == 1) {

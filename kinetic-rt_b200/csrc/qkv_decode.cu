@@ -162,12 +162,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           tma_load_5d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, 0, 0, 4 * head + half,
                       (kc0 + i) * KC, pol_w);
       };
-      // W tiles of the first stages do not depend on the prep kernel.
+      auto prefetch_w = [&](int i) {
+        if (TM == 128)
+          tma_prefetch_l2_3d(&tmap_w, 0, tile * 128, (kc0 + i) * KC);
+        else
+          tma_prefetch_l2_5d(&tmap_w, 0, 0, 0, 4 * head + half, (kc0 + i) * KC);
+      };
+      // W tiles of the first stages do not depend on the prep kernel; the
+      // next p.prefetch stages are requested into L2 beyond the ring.
       const int pre = nk < S ? nk : S;
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
         load_w(i, i);
       }
+      for (int i = pre; i < nk && i < pre + p.prefetch; ++i) prefetch_w(i);
       pdl_wait();
       for (int i = 0; i < pre; ++i)
         tma_load_3d(b_smem + (size_t)i * b_stage, &tmap_x, &tl->full[i], 0, 0, (kc0 + i) * KC, pol_x);
@@ -181,6 +189,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         mbar_arrive_expect_tx(&tl->full[s], stage_bytes);
         load_w(s, i);
         tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (kc0 + i) * KC, pol_x);
+        if (i + p.prefetch < nk) prefetch_w(i + p.prefetch);
       }
     }
   } else if (warp == 1) {

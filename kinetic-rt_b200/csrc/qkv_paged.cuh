@@ -37,6 +37,7 @@ struct PagedParams {
   int splits;         // split-K factor (decode)
   int stages;         // pipeline depth
   int kc;             // 64-column chunks per TMA box / pipeline stage
+  int prefetch;       // weight stages requested into L2 ahead of the shared-memory ring
   int tmem_cols;
   int* status;        // workspace status word
   int* counters;      // split-K arrival counters, one per head tile (decode)
