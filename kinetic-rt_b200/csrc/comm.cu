@@ -311,9 +311,10 @@ struct GemmCfg {
 // Tile height 128; 64 (twice the tiles, half the K splits and half the
 // exchange per split, but every tile re-reads X) is slower at every decode
 // shape measured on B200 (K = 512 .. 14336, N = 4096, 64 tokens) and only
-// runs when KRT_GEMM_TILE_M=64 asks for it.  Split-K factor = cluster size: as many splits
-// as fit (tiles * splits <= #SMs, at most 8) while every cluster can be
-// resident at once.
+// runs when KRT_GEMM_TILE_M=64 asks for it.  Split-K factor = cluster size:
+// as many splits as fit (tiles * splits <= #SMs, at most 8, at least four
+// 64-column blocks each) while every cluster can be resident at once.
+// KRT_GEMM_SPLITS overrides the split factor.
 GemmCfg gemm_config(int n_out, int num_kb, int n_pad) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, int, int>, GemmCfg> cache;
@@ -327,15 +328,20 @@ GemmCfg gemm_config(int n_out, int num_kb, int n_pad) {
   if (tile_m != 64) tile_m = 128;
   const int tiles = n_out / tile_m;
   GemmCfg cfg{tile_m, tiles, 1, 1, 1};
-  int s = device_sm_count() / tiles;
+  const int forced = env_int_value("KRT_GEMM_SPLITS", 0);
+  int s = forced > 0 ? forced : device_sm_count() / tiles;
   if (s > 8) s = 8;
+  // at least four 64-column blocks per split: shorter K ranges gain less
+  // streaming time than their partial exchange costs (measured on B200 at
+  // K = 512, N = 4096, 64 tokens: 2 splits 5.2 us, 4 splits 5.9 us)
+  if (forced <= 0 && s > num_kb / 4) s = num_kb / 4 > 0 ? num_kb / 4 : 1;
   if (s < 1) s = 1;
   for (; s >= 1; --s) {
     const int kc = gemm_kc(tile_m, num_kb, n_pad, s);
     const int st = gemm_stages(tile_m, n_pad, kc, s);
     if (st < 1 || s > num_kb / kc) continue;
     cfg = GemmCfg{tile_m, tiles, kc, st, s};
-    if (s == 1 || gemm_ar_max_active_clusters(tile_m, s, n_pad, st, kc) >= tiles) break;
+    if (forced > 0 || s == 1 || gemm_ar_max_active_clusters(tile_m, s, n_pad, st, kc) >= tiles) break;
   }
   cache[key] = cfg;
   return cfg;
