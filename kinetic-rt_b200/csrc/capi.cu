@@ -287,7 +287,10 @@ DecodeCfg decode_config(int heads, int num_kb, int n_pad) {
   const int tiles = heads * (128 / tile_m);
   DecodeCfg cfg{tile_m, tiles, 1, 1, 1};
   const int forced = env_int("KRT_DECODE_SPLITS", 0);
-  int s = forced > 0 ? forced : device_sm_count() / tiles;
+  // splits fill about two thirds of the SMs: more CTAs exchange more partials
+  // than their extra streaming gains (B200, 64 tokens: 24 half-head tiles
+  // x 4 splits 10.1 us, x 6 splits 10.6 us)
+  int s = forced > 0 ? forced : device_sm_count() * 2 / 3 / tiles;
   if (s > 8) s = 8;
   if (s < 1) s = 1;
   for (; s >= 1; --s) {
@@ -354,10 +357,11 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   p.kc = cfg.kc;
   p.stages = cfg.stages;
   p.splits = cfg.splits;
-  // L2 prefetch ahead of the ring for short K loops (at most 8 stages per
-  // CTA), where the ring alone cannot put enough weight bytes in flight
-  // early; long loops already keep HBM busy and only gain L2 pressure.
-  p.prefetch = env_int("KRT_L2_PREFETCH_STAGES", (num_kb / p.kc + p.splits - 1) / p.splits <= 8 ? 4 : 0);
+  // L2 prefetch of weight stages ahead of the ring: off by default.  It
+  // shortens the kernel alone (48 heads, 64 tokens: 16.4 -> 15.7 us) but
+  // lengthens a PDL-chained decoder-layer step on B200 (53.7 -> 54.9 us);
+  // KRT_L2_PREFETCH_STAGES turns it on.
+  p.prefetch = env_int("KRT_L2_PREFETCH_STAGES", 0);
   int cols = 32;
   while (cols < p.n_pad) cols <<= 1;
   p.tmem_cols = cols;

@@ -392,10 +392,10 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     p.kc = cfg.kc;
     p.stages = cfg.stages;
     p.splits = cfg.splits;
-    // L2 prefetch ahead of the ring for short K loops only (see the decode
-    // entry): measured on B200, o_proj (4 stages per CTA) 10.7 -> 10.3 us,
-    // down_proj (14 stages) unchanged or slower.
-    p.prefetch = env_int_value("KRT_L2_PREFETCH_STAGES", (num_kb / p.kc + p.splits - 1) / p.splits <= 8 ? 4 : 0);
+    // L2 prefetch of weight stages ahead of the ring: off by default (it
+    // shortens o_proj alone, 10.7 -> 10.3 us, but lengthens the chained
+    // decoder-layer step); KRT_L2_PREFETCH_STAGES turns it on.
+    p.prefetch = env_int_value("KRT_L2_PREFETCH_STAGES", 0);
     int cols = 32;
     while (cols < p.n_pad) cols <<= 1;
     p.tmem_cols = cols;
