@@ -311,7 +311,7 @@ extern "C" size_t krt_qkv_rope_decode_workspace_size(int32_t num_tokens, int32_t
   if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0 || head_dim != kHeadDim || n_heads <= 0 ||
       n_kv_heads <= 0)
     return 0;
-  return ws_layout(num_tokens, d_model, 0).total;
+  return ws_layout(num_tokens, d_model).total;
 }
 
 extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
@@ -366,7 +366,7 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   while (cols < p.n_pad) cols <<= 1;
   p.tmem_cols = cols;
   char* ws = static_cast<char*>(a->workspace);
-  const WsLayout L = ws_layout(p.num_tokens, p.d_model, 0);
+  const WsLayout L = ws_layout(p.num_tokens, p.d_model);
   p.status = reinterpret_cast<int*>(ws);
   p.tok_pos = reinterpret_cast<int*>(ws + L.pos_off);
   p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
@@ -399,7 +399,7 @@ extern "C" int krt_read_status(void* workspace, void* stream, int32_t* bits) {
   if (e != cudaSuccess) return cuda_error(e, "krt_read_status");
   *bits = v;
   if (v != 0) {
-    // An aborted launch can leave split-K counters behind: clear the header.
+    // Clear the status word (and the rest of the reserved header) for the next call.
     e = cudaMemsetAsync(workspace, 0, kWsHeaderBytes, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_error(e, "krt_read_status clear");
@@ -414,7 +414,7 @@ extern "C" size_t krt_qkv_rope_prefill_workspace_size(int32_t num_tokens, int32_
   (void)n_heads;
   (void)n_kv_heads;
   if (num_tokens <= 0 || d_model <= 0 || head_dim != kHeadDim) return 0;
-  return ws_layout(num_tokens, d_model, 0).total;
+  return ws_layout(num_tokens, d_model).total;
 }
 
 extern "C" int krt_qkv_rope_prefill(const krt_qkv_paged_args* a, void* stream) {
@@ -454,7 +454,7 @@ extern "C" int krt_qkv_rope_prefill(const krt_qkv_paged_args* a, void* stream) {
   p.tokens_per_block = a->tokens_per_block;
   p.eps = a->eps;
   char* ws = static_cast<char*>(a->workspace);
-  const WsLayout L = ws_layout(p.num_tokens, p.d_model, 0);
+  const WsLayout L = ws_layout(p.num_tokens, p.d_model);
   p.status = reinterpret_cast<int*>(ws);
   p.tok_pos = reinterpret_cast<int*>(ws + L.pos_off);
   p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);

@@ -15,7 +15,6 @@ namespace krt {
 
 constexpr int kMaxWorld = 8;
 constexpr int kArMaxCtas = 64;     // CTAs of the standalone allreduce
-constexpr int kChunkTokens = 16;   // token granularity of the fused exchange
 constexpr int kMaxChunks = 16;     // 256 tokens per launch
 
 struct CommLayout {

@@ -227,13 +227,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
 
-// Byte offset of element (row, k) inside a [rows x 64] bf16 tile stored with
-// the 128-byte swizzle (what TMA writes for a 128-byte inner box).
-__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t k) {
-  const uint32_t chunk = (k >> 3) ^ (row & 7);
-  return row * 128u + (chunk << 4) + ((k & 7) << 1);
-}
-
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -279,21 +272,6 @@ __device__ __forceinline__ uint64_t ll_word(uint32_t payload, uint32_t epoch) {
 }
 __device__ __forceinline__ void st_ll2(uint64_t* dst, uint64_t a, uint64_t b) {
   asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
-}
-// Poll two words until both carry `epoch`; false once the wait budget,
-// counted from t0, is spent.
-__device__ __forceinline__ bool poll_ll2(const uint64_t* src, uint32_t epoch, uint64_t t0, uint32_t& a,
-                                         uint32_t& b) {
-  while (true) {
-    uint64_t x, y;
-    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(src) : "memory");
-    if ((uint32_t)(x >> 32) == epoch && (uint32_t)(y >> 32) == epoch) {
-      a = (uint32_t)x;
-      b = (uint32_t)y;
-      return true;
-    }
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
-  }
 }
 
 // 24-bit float: fp32 rounded to nearest-even at mantissa bit 8 (sign,
@@ -377,11 +355,6 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// All threads of all CTAs of the cluster; release/acquire orders shared
-// memory writes before the barrier with reads of them after it.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
 // Split cluster barrier: arrive early (after the mbarrier inits), wait
 // later, right before the first access to another CTA's shared memory.
 __device__ __forceinline__ void cluster_arrive_relaxed() {
@@ -410,15 +383,6 @@ __device__ __forceinline__ uint32_t map_smem_to_rank(uint32_t smem_addr, uint32_
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
 }
-// No memory clobber: the loads stay ordered after the (volatile) cluster
-// barrier but may be issued back to back, so their latencies overlap.
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr));
-  return v;
-}
 
 // ------------------------------------------------------- cross-GPU flags
 // Flags live in symmetric buffers that peers write over NVLink.  A producer
@@ -432,9 +396,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Orders this thread's earlier memory operations, and those of threads that
-// synchronised with it through a barrier, before its later ones, system-wide.
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 // Wait until *flag == expect; false after kWaitBudgetNs.
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t expect) {
   if (ld_acquire_sys(flag) == expect) return true;

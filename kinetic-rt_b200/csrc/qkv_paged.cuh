@@ -12,9 +12,8 @@ constexpr int kHeadDim = 128;   // tile rows = one head of Q, K or V
 constexpr int kBK = 64;         // k elements per pipeline stage (128-byte rows)
 constexpr int kMaxStages = 8;
 
-// Workspace header: [0] status word, [64 .. 64 + 4*kMaxTiles) split-K counters.
-constexpr int kMaxTiles = 1024;
-constexpr size_t kWsCounterOffset = 64;
+// Workspace header: [0] status word; the rest of the first 8 KB is reserved.
+constexpr int kMaxTiles = 1024;  // head tiles per call
 constexpr size_t kWsHeaderBytes = 8192;
 
 struct PagedParams {
@@ -40,25 +39,22 @@ struct PagedParams {
   int prefetch;       // weight stages requested into L2 ahead of the shared-memory ring
   int tmem_cols;
   int* status;        // workspace status word
-  int* counters;      // split-K arrival counters, one per head tile (decode)
   int* tok_pos;       // [num_tokens] position, or -1 when outside the RoPE table
   long long* tok_slot;  // [num_tokens] pool slot, or -1 when the block lookup failed
   __nv_bfloat16* xhat;  // [num_tokens, d_model] bf16(x * rsqrt(mean(x^2)+eps) * gamma)
-  float* partial;     // [tiles][splits][128][n_pad] split-K partial sums (decode)
 };
 
 // Workspace layout shared by the decode and prefill paths.
 struct WsLayout {
-  size_t pos_off, slot_off, xhat_off, partial_off, total;
+  size_t pos_off, slot_off, xhat_off, total;
 };
-inline WsLayout ws_layout(int T, int D, size_t partial_bytes) {
+inline WsLayout ws_layout(int T, int D) {
   auto up = [](size_t v) { return (v + 1023) & ~size_t(1023); };
   WsLayout l;
   l.pos_off = kWsHeaderBytes;
   l.slot_off = up(l.pos_off + 4 * (size_t)T);
   l.xhat_off = up(l.slot_off + 8 * (size_t)T);
-  l.partial_off = up(l.xhat_off + 2 * (size_t)T * D);
-  l.total = l.partial_off + partial_bytes;
+  l.total = up(l.xhat_off + 2 * (size_t)T * D);
   return l;
 }
 
