@@ -217,10 +217,16 @@ KRT_API int krt_allreduce(krt_comm* comm, const void* send, void* recv, size_t c
  * Rank r holds W[:, K_r] and X[:, K_r] (the torch.chunk(dim=1) shards of
  * scripts/export_hf.py:62-65); every rank receives
  *   Y = sum_r X[:, K_r] W[:, K_r]^T          (bf16 out, fp32 accumulation)
- * in one call: tcgen05 GEMM whose epilogue reduce-scatters fp32 partials into
- * the owners' peer buffers and all-gathers the bf16 result, with no separate
- * collective.  comm may be NULL for a single GPU.  Any num_tokens (launched
- * in slices of 256); k_local % 64 == 0, n_out % 128 == 0.
+ * in one call: a tcgen05 GEMM whose epilogue exchanges the partial products
+ * through the ranks' peer buffers (two ranks: each sends its partial to the
+ * other and both reduce; more ranks: reduce-scatter to the owner of each
+ * 128-feature tile, then all-gather of the bf16 result), with no separate
+ * collective.  Partials travel as fp32 rounded to 15-bit mantissas and are
+ * summed in fp32 in rank order, so every rank gets bit-identical results.
+ * comm may be NULL for a single GPU.  Any num_tokens (launched in slices of
+ * 256); k_local % 64 == 0, n_out % 128 == 0.  Calls that share a
+ * communicator must be made in the same order, with the same shapes, on
+ * every rank.
  * ---------------------------------------------------------------------- */
 typedef struct krt_gemm_ar_args {
   const void* x;      /* bf16 [num_tokens, k_local], row stride x_stride */
