@@ -141,6 +141,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nk = kc1 - kc0;
   const int row0 = tile * TM;
 
+  const int pre = nk < S ? nk : S;  // stages loaded before the ring turns over
+  uint64_t pol_w = 0;                // thread 0 = the TMA producer
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&tl->full[s], 1);
@@ -150,10 +152,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&tl->recv, 1);
     tl->abort = 0;
     fence_mbar_init();
+    // The weight tiles of the first stages depend on nothing: request them
+    // before TMEM allocation and the block barrier.
+    tma_prefetch_desc(&tmap_w);
+    pol_w = make_l2_policy_evict_first();  // weights are streamed once
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
+      tma_load_3d(a_smem + (size_t)i * a_stage, &tmap_w, &tl->full[i], 0, row0, (kc0 + i) * KC, pol_w);
+    }
+    // the next p.prefetch weight stages are requested into L2 beyond the ring
+    for (int i = pre; i < nk && i < pre + p.prefetch; ++i) tma_prefetch_l2_3d(&tmap_w, 0, row0, (kc0 + i) * KC);
     // the partials this CTA will receive: (splits - 1) per owned chunk
     mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
                                          TS::kChunkBytes);
-    tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
@@ -172,15 +183,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol_w = make_l2_policy_evict_first();
       const uint64_t pol_x = make_l2_policy_evict_last();
-      const int pre = nk < S ? nk : S;
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
-        tma_load_3d(a_smem + (size_t)i * a_stage, &tmap_w, &tl->full[i], 0, row0, (kc0 + i) * KC, pol_w);
-      }
-      // the next p.prefetch weight stages are requested into L2 beyond the ring
-      for (int i = pre; i < nk && i < pre + p.prefetch; ++i) tma_prefetch_l2_3d(&tmap_w, 0, row0, (kc0 + i) * KC);
       pdl_wait();  // X may come from the previous kernel
       for (int i = 0; i < pre; ++i)
         tma_load_3d(b_smem + (size_t)i * b_stage, &tmap_x, &tl->full[i], 0, 0, (kc0 + i) * KC, pol_x);

@@ -117,6 +117,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   const int kc1 = (int)((long long)(split + 1) * num_kc / p.splits);
   const int nk = kc1 - kc0;  // pipeline stages (KC chunks each) of this CTA
 
+  const int pre = nk < S ? nk : S;  // stages loaded before the ring turns over
+  uint64_t pol_w = 0;                // thread 0 = the TMA producer
+  auto load_w = [&](int s, int i) {
+    if (TM == 128)
+      tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, tile * 128, (kc0 + i) * KC, pol_w);
+    else
+      tma_load_5d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, 0, 0, 4 * head + half, (kc0 + i) * KC,
+                  pol_w);
+  };
+  auto prefetch_w = [&](int i) {
+    if (TM == 128)
+      tma_prefetch_l2_3d(&tmap_w, 0, tile * 128, (kc0 + i) * KC);
+    else
+      tma_prefetch_l2_5d(&tmap_w, 0, 0, 0, 4 * head + half, (kc0 + i) * KC);
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&tl->full[s], 1);
@@ -126,10 +141,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     mbar_init(&tl->recv, 1);
     tl->abort = 0;
     fence_mbar_init();
+    // The weight tiles of the first stages depend on nothing (not even the
+    // prep kernel): request them before TMEM allocation and the block
+    // barrier; the next p.prefetch stages go to L2 beyond the ring.
+    tma_prefetch_desc(&tmap_w);
+    pol_w = make_l2_policy_evict_first();  // weights are streamed once
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
+      load_w(i, i);
+    }
+    for (int i = pre; i < nk && i < pre + p.prefetch; ++i) prefetch_w(i);
     // the partials this CTA will receive: (splits - 1) per owned chunk
     mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
                                          TS::kChunkBytes);
-    tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
@@ -153,29 +177,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint64_t pol_w = make_l2_policy_evict_first();  // weights are streamed once
-      const uint64_t pol_x = make_l2_policy_evict_last();   // x_hat is re-read by every tile
-      auto load_w = [&](int s, int i) {
-        if (TM == 128)
-          tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, tile * 128, (kc0 + i) * KC, pol_w);
-        else
-          tma_load_5d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, 0, 0, 4 * head + half,
-                      (kc0 + i) * KC, pol_w);
-      };
-      auto prefetch_w = [&](int i) {
-        if (TM == 128)
-          tma_prefetch_l2_3d(&tmap_w, 0, tile * 128, (kc0 + i) * KC);
-        else
-          tma_prefetch_l2_5d(&tmap_w, 0, 0, 0, 4 * head + half, (kc0 + i) * KC);
-      };
-      // W tiles of the first stages do not depend on the prep kernel; the
-      // next p.prefetch stages are requested into L2 beyond the ring.
-      const int pre = nk < S ? nk : S;
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&tl->full[i], stage_bytes);
-        load_w(i, i);
-      }
-      for (int i = pre; i < nk && i < pre + p.prefetch; ++i) prefetch_w(i);
+      const uint64_t pol_x = make_l2_policy_evict_last();  // x_hat is re-read by every tile
       pdl_wait();
       for (int i = 0; i < pre; ++i)
         tma_load_3d(b_smem + (size_t)i * b_stage, &tmap_x, &tl->full[i], 0, 0, (kc0 + i) * KC, pol_x);
