@@ -264,8 +264,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (remote) {
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
-        if (ept == 0) {
-          for (int cc = 0; cc < nc; ++cc) {
+        // chunk cc of the group is sent by lane 0 of epilogue warp cc, so the
+        // (remote) bulk-copy issues of a group run in parallel
+        if ((ept & 31) == 0) {
+          for (int cc = ept >> 5; cc < nc; cc += 4) {
             const int c = c0 + cc, cowner = c % nranks;
             if (cowner == crank) continue;
             const int slot = recv_slot(c / nranks, nranks, cowner, crank);
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
-    if (ept == 0) bulk_commit_group();
+    if ((ept & 31) == 0) bulk_commit_group();
     named_bar_sync(1, 128);  // the owned chunks are parked
     const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
     if (!got && lane == 0) gemm_fail(p, tl, kStatusTimeoutCluster);
@@ -421,7 +423,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok) atomicOr(p.status, kStatusTimeoutPeer);
     }
-    if (ept == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
+    if ((ept & 31) == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }
 
   if (warp < 2) cluster_wait();

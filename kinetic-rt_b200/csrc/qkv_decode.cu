@@ -282,8 +282,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       if (remote) {
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
-        if (ept == 0) {
-          for (int cc = 0; cc < nc; ++cc) {
+        // chunk cc of the group is sent by lane 0 of epilogue warp cc, so the
+        // (remote) bulk-copy issues of a group run in parallel
+        if ((ept & 31) == 0) {
+          for (int cc = ept >> 5; cc < nc; cc += 4) {
             const int c = c0 + cc, owner = c % nranks;
             if (owner == rank) continue;
             const int slot = recv_slot(c / nranks, nranks, owner, rank);
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         }
       }
     }
-    if (ept == 0) bulk_commit_group();
+    if ((ept & 31) == 0) bulk_commit_group();
     named_bar_sync(1, 128);  // the owned chunks are parked
 
     // ------------------------------------------------ finish the owned chunks
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         store_rows_n<RG>(p, head, t, hr0, sign, pos, tl->slot[t], y, yp, cs, sn);
       }
     }
-    if (ept == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
+    if ((ept & 31) == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }
 
   if (warp < 2) cluster_wait();
