@@ -312,15 +312,16 @@ struct GemmCfg {
 // exchange per split, but every tile re-reads X) is slower at every decode
 // shape measured on B200 (K = 512 .. 14336, N = 4096, 64 tokens) and only
 // runs when KRT_GEMM_TILE_M=64 asks for it.  Split-K factor = cluster size:
-// as many splits as fit (tiles * splits <= #SMs, at most 8, at least four
-// 64-column blocks each) while every cluster can be resident at once.
+// as many splits as fit (tiles * splits <= #SMs, at most 8, on one GPU at
+// least four 64-column blocks each) while every cluster can be resident at
+// once.
 // KRT_GEMM_SPLITS overrides the split factor.
-GemmCfg gemm_config(int n_out, int num_kb, int n_pad) {
+GemmCfg gemm_config(int n_out, int num_kb, int n_pad, int world) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int>, GemmCfg> cache;
+  static std::map<std::tuple<int, int, int, int, int>, GemmCfg> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, n_out, num_kb, n_pad);
+  const auto key = std::make_tuple(dev, n_out, num_kb, n_pad, world);
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
@@ -331,10 +332,13 @@ GemmCfg gemm_config(int n_out, int num_kb, int n_pad) {
   const int forced = env_int_value("KRT_GEMM_SPLITS", 0);
   int s = forced > 0 ? forced : device_sm_count() / tiles;
   if (s > 8) s = 8;
-  // at least four 64-column blocks per split: shorter K ranges gain less
-  // streaming time than their partial exchange costs (measured on B200 at
-  // K = 512, N = 4096, 64 tokens: 2 splits 5.2 us, 4 splits 5.9 us)
-  if (forced <= 0 && s > num_kb / 4) s = num_kb / 4 > 0 ? num_kb / 4 : 1;
+  // On one GPU, at least four 64-column blocks per split: shorter K ranges
+  // gain less streaming time than their partial exchange costs (B200,
+  // K = 512, N = 4096, 64 tokens: 2 splits 5.2 us, 4 splits 5.9 us).  With
+  // a fused allreduce, fewer splits leave each CTA more chunks to exchange
+  // across GPUs one after another (8 GPUs, K = 512: 2 splits 19.6 us,
+  // 4 splits 14.1 us), so all splits stay.
+  if (forced <= 0 && world == 1 && s > num_kb / 4) s = num_kb / 4 > 0 ? num_kb / 4 : 1;
   if (s < 1) s = 1;
   for (; s >= 1; --s) {
     const int kc = gemm_kc(tile_m, num_kb, n_pad, s);
@@ -388,7 +392,7 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
     p.num_tokens = T;
     p.n_pad = (T + 15) / 16 * 16;
-    const GemmCfg cfg = gemm_config(a->n_out, num_kb, p.n_pad);
+    const GemmCfg cfg = gemm_config(a->n_out, num_kb, p.n_pad, p.comm.world);
     p.kc = cfg.kc;
     p.stages = cfg.stages;
     p.splits = cfg.splits;
