@@ -262,6 +262,32 @@ def barrier(torch, world):
     torch.cuda.synchronize()
 
 
+def parse_cpulist(text):
+    """CPU ids of a sysfs cpulist string ("0-3,8,10-11")."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def gpu_local_cpus(torch, device, sysfs="/sys/bus/pci/devices"):
+    """The allowed CPUs on the GPU's own NUMA node (the local_cpulist of its
+    PCI function in sysfs), or None when that is unknown or covers them all."""
+    try:
+        p = torch.cuda.get_device_properties(device)
+        path = f"{sysfs}/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/local_cpulist"
+        with open(path) as f:
+            local = parse_cpulist(f.read())
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return None
+    allowed = os.sched_getaffinity(0)
+    local &= allowed
+    return local if local and local != allowed else None
+
+
 STEPS_PER_GRAPH = 8
 
 
@@ -355,7 +381,13 @@ def run_krt(args, rank, world, local_rank):
     # activations from pinned host memory, runs the three calls and copies q
     # and both layer outputs back.  Two input/output sets alternate so that a
     # step's copies overlap its neighbours' kernels (H2D and D2H on their own
-    # streams); 8 steps per CUDA graph.
+    # streams); 8 steps per CUDA graph.  The pinned buffers are allocated, and
+    # the graphs launched, from the CPUs of the GPU's own NUMA node: pinned
+    # pages on the far socket cross the inter-socket link on every copy.
+    saved_cpus = os.sched_getaffinity(0)
+    local_cpus = gpu_local_cpus(torch, local_rank)
+    if local_cpus:
+        os.sched_setaffinity(0, local_cpus)
     ios = [rig.io_set(), rig.io_set()]
     pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())
     h_in = [{k: pin(io[k]) for k in ("x", "attn", "act")} for io in ios]
@@ -420,6 +452,7 @@ def run_krt(args, rank, world, local_rank):
     b.record()
     barrier(torch, world)
     e2e_ms = max_over_ranks(torch, a.elapsed_time(b), world) / e2e_steps
+    os.sched_setaffinity(0, saved_cpus)  # the CPU baseline below uses every allowed core
     rig.check_status()
     for io in ios:
         rc, bits = rig.lib.read_status(io["ws_qkv"])
@@ -434,7 +467,9 @@ def run_krt(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights and activations)", "config": workload_config(world),
             "e2e": {"value": round(BATCH / (e2e_ms * 1e-3), 1), "unit": "tokens/s (one decoder layer's hot path)",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "host_cpus": (f"{len(local_cpus)} on the GPU's NUMA node" if local_cpus
+                                  else f"all {len(saved_cpus)} allowed")},
             "gpu_launches": rig.launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "kernel": dominant["kernel"], "achieved": dominant["achieved"],
                          "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["frac"],

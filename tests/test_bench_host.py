@@ -1,0 +1,35 @@
+"""Host-side helpers of bench.py (no GPU): the NUMA-local CPU set that the
+end-to-end measurement binds to while it allocates pinned buffers and
+launches its graphs."""
+import os
+import types
+
+import bench
+
+
+def test_parse_cpulist():
+    assert bench.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert bench.parse_cpulist("5") == {5}
+    assert bench.parse_cpulist("") == set()
+
+
+def _fake_torch(domain, bus, dev):
+    props = types.SimpleNamespace(pci_domain_id=domain, pci_bus_id=bus, pci_device_id=dev)
+    return types.SimpleNamespace(cuda=types.SimpleNamespace(get_device_properties=lambda d: props))
+
+
+def test_gpu_local_cpus_reads_the_gpu_pci_function(tmp_path):
+    allowed = sorted(os.sched_getaffinity(0))
+    fn = tmp_path / "0000:1b:00.0"
+    fn.mkdir()
+    # a node holding only the first allowed CPU (plus one that is not allowed)
+    (fn / "local_cpulist").write_text(f"{allowed[0]},{max(allowed) + 1000}\n")
+    got = bench.gpu_local_cpus(_fake_torch(0, 0x1B, 0), 0, sysfs=str(tmp_path))
+    if len(allowed) == 1:
+        assert got is None            # the node covers every allowed CPU: nothing to bind
+    else:
+        assert got == {allowed[0]}
+
+
+def test_gpu_local_cpus_unknown_device(tmp_path):
+    assert bench.gpu_local_cpus(_fake_torch(0, 0x2A, 0), 0, sysfs=str(tmp_path)) is None
