@@ -387,7 +387,10 @@ def run_krt(args, rank, world, local_rank):
     saved_cpus = os.sched_getaffinity(0)
     local_cpus = gpu_local_cpus(torch, local_rank)
     if local_cpus:
-        os.sched_setaffinity(0, local_cpus)
+        try:
+            os.sched_setaffinity(0, local_cpus)
+        except OSError:
+            local_cpus = None
     ios = [rig.io_set(), rig.io_set()]
     pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())
     h_in = [{k: pin(io[k]) for k in ("x", "attn", "act")} for io in ios]
@@ -452,7 +455,8 @@ def run_krt(args, rank, world, local_rank):
     b.record()
     barrier(torch, world)
     e2e_ms = max_over_ranks(torch, a.elapsed_time(b), world) / e2e_steps
-    os.sched_setaffinity(0, saved_cpus)  # the CPU baseline below uses every allowed core
+    if local_cpus:
+        os.sched_setaffinity(0, saved_cpus)  # the CPU baseline below uses every allowed core
     rig.check_status()
     for io in ios:
         rc, bits = rig.lib.read_status(io["ws_qkv"])
