@@ -381,7 +381,9 @@ def run_krt(args, rank, world, local_rank):
     # activations from pinned host memory, runs the three calls and copies q
     # and both layer outputs back.  Two input/output sets alternate so that a
     # step's copies overlap its neighbours' kernels (H2D and D2H on their own
-    # streams); 8 steps per CUDA graph.  The pinned buffers are allocated, and
+    # streams).  One CUDA graph holds a whole number of passes over the layers
+    # and at least 48 steps, since the pipeline drains where a graph ends (its
+    # side streams join the main one).  The pinned buffers are allocated, and
     # the graphs launched, from the CPUs of the GPU's own NUMA node: pinned
     # pages on the far socket cross the inter-socket link on every copy.
     saved_cpus = os.sched_getaffinity(0)
@@ -400,6 +402,9 @@ def run_krt(args, rank, world, local_rank):
     d2h = sum(t.numel() * t.element_size() for t in h_out[0].values())
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
 
+    passes = -(-48 // rig.n_layers)
+    e2e_per_graph = rig.n_layers * passes  # a graph starts at layer 0 and ends at the last layer
+
     def e2e_steps_captured(first):
         comp = torch.cuda.current_stream()
         ev = lambda: torch.cuda.Event()
@@ -408,7 +413,7 @@ def run_krt(args, rank, world, local_rank):
         fork.record(comp)
         s_in.wait_event(fork)
         s_out.wait_event(fork)
-        for i in range(first, first + STEPS_PER_GRAPH):
+        for i in range(first, first + e2e_per_graph):
             b = i % 2
             with torch.cuda.stream(s_in):
                 if i - 2 in done_comp:
@@ -438,20 +443,16 @@ def run_krt(args, rank, world, local_rank):
         e2e_steps_captured(0)  # eager warm-up of the same sequence
     torch.cuda.current_stream().wait_stream(cap)
     torch.cuda.synchronize()
-    e2e_graphs = []
-    for k in range(rig.n_layers):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            e2e_steps_captured(k * STEPS_PER_GRAPH)
-        e2e_graphs.append(g)
-    e2e_steps = STEPS_PER_GRAPH * max(4, min(args.steps, 800) // STEPS_PER_GRAPH)
-    for g in e2e_graphs:
-        g.replay()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
+        e2e_steps_captured(0)
+    e2e_steps = e2e_per_graph * max(2, min(args.steps, 800) // e2e_per_graph)
+    e2e_graph.replay()
     barrier(torch, world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(e2e_steps // STEPS_PER_GRAPH):
-        e2e_graphs[i % len(e2e_graphs)].replay()
+    for _ in range(e2e_steps // e2e_per_graph):
+        e2e_graph.replay()
     b.record()
     barrier(torch, world)
     e2e_ms = max_over_ranks(torch, a.elapsed_time(b), world) / e2e_steps
@@ -485,7 +486,7 @@ def run_krt(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
     if comm is not None:
         import torch.distributed as dist
-        del graphs, e2e_graphs
+        del graphs, e2e_graph
         torch.cuda.synchronize()
         comm.close()
         dist.barrier()
