@@ -33,3 +33,25 @@ def test_gpu_local_cpus_reads_the_gpu_pci_function(tmp_path):
 
 def test_gpu_local_cpus_unknown_device(tmp_path):
     assert bench.gpu_local_cpus(_fake_torch(0, 0x2A, 0), 0, sysfs=str(tmp_path)) is None
+
+
+def test_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` (the CPU path, no GPU) prints one JSON line
+    with the keys the driver reads, on the same metric and config as the
+    GPU arm."""
+    import json
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["value"] > 0
+    assert d["config"] == bench.workload_config(1)
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["cpu_baseline"]["kind"] == "port"
