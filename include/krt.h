@@ -240,6 +240,43 @@ typedef struct krt_gemm_ar_args {
 KRT_API size_t krt_rowparallel_gemm_ar_workspace_size(void);
 KRT_API int krt_rowparallel_gemm_ar(krt_comm* comm, const krt_gemm_ar_args* args, void* stream);
 
+/* -------------------------------------------------------------------------
+ * Paged decode attention (one query token per sequence, bf16, GQA).
+ *
+ * No kernel in the reference: its decoder forward does not exist yet
+ * (python/kinetic_rt/orchestrator.py:419-448 re-runs the model per token);
+ * this is the attention that reads the pool BlockManager owns
+ * (include/BlockManager.h:29-95) after krt_qkv_rope_decode wrote the token's
+ * K/V there.  For sequence s and query head h:
+ *   out[s, h] = softmax(scale * q[s, h] . K^T) V  over tokens 0 .. seq_lens[s]-1
+ * with K/V of KV head h / (n_heads / n_kv_heads), token p at pool slot
+ * block_table[s * block_table_stride + p / tokens_per_block] * tokens_per_block
+ * + p % tokens_per_block (token layout [K | V][kv_head][128] bf16).  fp32
+ * accumulation and softmax; head_dim 128; at most 16 query heads per KV head;
+ * tokens_per_block a multiple of 16.  A sequence with seq_lens <= 0 gets
+ * zeros.  Out-of-range block ids are masked and set status bit 8.  The
+ * workspace (krt_paged_attention_workspace_size bytes) is zero-filled once
+ * when allocated; the kernel leaves its counters at zero after every call.
+ * ---------------------------------------------------------------------- */
+typedef struct krt_paged_attention_args {
+  const void* q;              /* bf16 [num_seqs, q_stride], query head h at h * 128 */
+  const void* kv_pool;        /* bf16, num_blocks * tokens_per_block * token_bytes bytes */
+  const int32_t* block_table; /* [num_seqs, block_table_stride] */
+  const int32_t* seq_lens;    /* [num_seqs] tokens attended, the current one included */
+  void* out;                  /* bf16 [num_seqs, out_stride] */
+  int32_t num_seqs, n_heads, n_kv_heads, head_dim;
+  int32_t q_stride, out_stride;
+  int32_t block_table_stride, num_blocks, tokens_per_block;
+  int32_t max_seq_len; /* upper bound of seq_lens: sizes the grid and the workspace */
+  float scale;         /* softmax scale; 0 = 1 / sqrt(head_dim) */
+  void* workspace;
+  size_t workspace_bytes;
+} krt_paged_attention_args;
+
+KRT_API size_t krt_paged_attention_workspace_size(int32_t num_seqs, int32_t n_heads, int32_t n_kv_heads,
+                                                  int32_t max_seq_len);
+KRT_API int krt_paged_attention_decode(const krt_paged_attention_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -135,6 +136,37 @@ int make_tmap_bf16_half_heads(CUtensorMap* map, const void* base, int heads, uin
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled (5-D) failed (CUresult %d)", (int)r);
+  return KRT_OK;
+}
+
+// bf16 tensor map of any rank <= 5 with explicit byte strides (dims[0] is
+// contiguous, the other strides in any order, multiples of 16), 128-byte
+// swizzle (box[0] * 2 must be 128 bytes).
+int make_tmap_bf16_5d_strided(CUtensorMap* map, const void* base, std::initializer_list<uint64_t> dims,
+                              std::initializer_list<uint64_t> strides, std::initializer_list<uint32_t> box) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(KRT_ERR_INVALID, "TMA base address must be 16-byte aligned");
+  const int rank = (int)dims.size();
+  if (rank < 2 || rank > 5 || (int)strides.size() != rank - 1 || (int)box.size() != rank)
+    return set_error(KRT_ERR_INVALID, "tensor map: inconsistent rank");
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  int i = 0;
+  for (uint64_t v : dims) d[i++] = v;
+  i = 0;
+  for (uint64_t v : strides) {
+    if (v % 16 != 0) return set_error(KRT_ERR_INVALID, "tensor map: strides must be multiples of 16 bytes");
+    st[i++] = v;
+  }
+  i = 0;
+  for (uint32_t v : box) bx[i++] = v;
+  for (i = 0; i < rank; ++i) es[i] = 1;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KRT_ERR_CUDA, "cuTensorMapEncodeTiled (%d-D) failed (CUresult %d)", rank, (int)r);
   return KRT_OK;
 }
 

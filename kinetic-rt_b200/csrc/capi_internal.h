@@ -6,6 +6,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <initializer_list>
 
 namespace krt {
 
@@ -18,6 +19,8 @@ int clear_error();
 int device_sm_count();
 int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                       uint32_t box_rows, uint32_t kc);
+int make_tmap_bf16_5d_strided(CUtensorMap* map, const void* base, std::initializer_list<uint64_t> dims,
+                              std::initializer_list<uint64_t> strides, std::initializer_list<uint32_t> box);
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                       uint32_t box_rows);
 

@@ -62,6 +62,18 @@ class GemmArArgs(ctypes.Structure):
     ]
 
 
+class PagedAttentionArgs(ctypes.Structure):
+    """krt_paged_attention_args"""
+    _fields_ = [
+        ("q", _vp), ("kv_pool", _vp), ("block_table", _vp), ("seq_lens", _vp), ("out", _vp),
+        ("num_seqs", _i32), ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32),
+        ("q_stride", _i32), ("out_stride", _i32),
+        ("block_table_stride", _i32), ("num_blocks", _i32), ("tokens_per_block", _i32),
+        ("max_seq_len", _i32), ("scale", ctypes.c_float),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 # Every symbol include/krt.h declares, with (restype, argtypes).
 SIGNATURES = {
     "krt_last_error": (ctypes.c_char_p, []),
@@ -81,6 +93,8 @@ SIGNATURES = {
     "krt_allreduce": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t, _i32, _vp, _vp]),
     "krt_rowparallel_gemm_ar_workspace_size": (ctypes.c_size_t, []),
     "krt_rowparallel_gemm_ar": (ctypes.c_int, [_vp, ctypes.POINTER(GemmArArgs), _vp]),
+    "krt_paged_attention_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
+    "krt_paged_attention_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttentionArgs), _vp]),
 }
 
 _lib = None
@@ -248,3 +262,27 @@ def gemm_ar_args(x, weight, y, workspace):
 
 def rowparallel_gemm_ar(comm, args, stream=None):
     check(lib().krt_rowparallel_gemm_ar(comm, ctypes.byref(args), _stream(stream)))
+
+
+# ------------------------------------------------------- paged attention
+def attention_workspace_bytes(num_seqs, n_heads, n_kv_heads, max_seq_len):
+    return int(lib().krt_paged_attention_workspace_size(num_seqs, n_heads, n_kv_heads, max_seq_len))
+
+
+def attention_args(q, kv_pool, block_table, seq_lens, out, n_heads, n_kv_heads, num_blocks, tokens_per_block,
+                   max_seq_len, workspace, scale=0.0, head_dim=128):
+    """q / out: bf16 [num_seqs, >= n_heads * 128]; kv_pool: this layer's pool."""
+    a = PagedAttentionArgs()
+    a.q, a.kv_pool, a.block_table, a.seq_lens, a.out = (_ptr(q), _ptr(kv_pool), _ptr(block_table), _ptr(seq_lens),
+                                                        _ptr(out))
+    a.num_seqs, a.n_heads, a.n_kv_heads, a.head_dim = int(q.shape[0]), int(n_heads), int(n_kv_heads), int(head_dim)
+    a.q_stride, a.out_stride = int(q.stride(0)), int(out.stride(0))
+    a.block_table_stride, a.num_blocks = int(block_table.stride(0)), int(num_blocks)
+    a.tokens_per_block, a.max_seq_len, a.scale = int(tokens_per_block), int(max_seq_len), float(scale)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel() * workspace.element_size()
+    return a
+
+
+def paged_attention_decode(args, stream=None):
+    check(lib().krt_paged_attention_decode(ctypes.byref(args), _stream(stream)))

@@ -11,6 +11,8 @@ Modules:
                   (include/BlockManager.h:29-95, src/GraphWrapper.cpp:139-145).
   gemm_ar      -- row-parallel sharding (scripts/export_hf.py:62-65) and the
                   allreduce-sum semantics (tests/mock_rccl.h:27-76).
+  attention    -- paged decode attention over the pool layout above (no
+                  reference counterpart; standard GQA scaled-dot-product).
   bf16         -- bfloat16 <-> float32 conversion with round-to-nearest-even.
 
 Parity pins: tests/golden/ holds vectors produced by the reference's own
