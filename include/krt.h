@@ -235,6 +235,11 @@ typedef struct krt_gemm_ar_args {
   int32_t num_tokens, k_local, n_out, x_stride, y_stride;
   void* workspace;    /* krt_rowparallel_gemm_ar_workspace_size() bytes, zeroed once */
   size_t workspace_bytes;
+  /* Optional residual (NULL = none): Y = residual + sum_r X_r W_r^T, summed
+   * in fp32 before the one bf16 rounding, as the decoder's residual stream
+   * h = h + o_proj(attn) / h + down_proj(act).  bf16, same row stride as y,
+   * identical on every rank; it may be y itself (updated in place). */
+  const void* residual;
 } krt_gemm_ar_args;
 
 KRT_API size_t krt_rowparallel_gemm_ar_workspace_size(void);
@@ -276,6 +281,81 @@ typedef struct krt_paged_attention_args {
 KRT_API size_t krt_paged_attention_workspace_size(int32_t num_seqs, int32_t n_heads, int32_t n_kv_heads,
                                                   int32_t max_seq_len);
 KRT_API int krt_paged_attention_decode(const krt_paged_attention_args* args, void* stream);
+
+/* -------------------------------------------------------------------------
+ * The rest of a decode step (batch of up to 256 tokens, bf16, fp32
+ * accumulation).  The reference has no decoder forward; these are the
+ * callers on either side of the hot path that its generation loop
+ * (python/kinetic_rt/orchestrator.py:419-448, argmax at 442-444) needs, in
+ * Llama's layer order: RMSNorm -> QKV + RoPE (krt_qkv_rope_decode) ->
+ * attention -> o_proj + allreduce + residual -> RMSNorm -> gate/up + SwiGLU
+ * -> down_proj + allreduce + residual; after the last layer RMSNorm ->
+ * lm_head -> greedy argmax -> embedding of the chosen tokens.
+ *
+ * Both projections below normalise x first (RMSNorm with rms_weight, the
+ * same cast-back order as the QKV path) and use a workspace of
+ * krt_projection_workspace_size() bytes.
+ * ---------------------------------------------------------------------- */
+KRT_API size_t krt_projection_workspace_size(int32_t num_tokens, int32_t d_model);
+
+/* act = silu(x_hat W_gate^T) * (x_hat W_up^T), column-parallel over the
+ * intermediate features (this rank's inter_local of them).  The weight keeps
+ * gate and up rows side by side in 64-row groups: rows 128 i .. 128 i + 63
+ * are gate rows of features 64 i .. 64 i + 63 and the next 64 rows are the up
+ * rows of the same features (a load-time interleave of the two shards). */
+typedef struct krt_gate_up_args {
+  const void* x;              /* bf16 [num_tokens, d_model], row stride x_stride */
+  const void* rms_weight;     /* bf16 [d_model] */
+  const void* gate_up_weight; /* bf16 [2 * inter_local, d_model], interleaved as above */
+  void* act;                  /* bf16 [num_tokens, act_stride] */
+  int32_t num_tokens, d_model, inter_local, x_stride, act_stride;
+  float eps;
+  void* workspace;
+  size_t workspace_bytes;
+} krt_gate_up_args;
+KRT_API int krt_gate_up_swiglu(const krt_gate_up_args* args, void* stream);
+
+/* Greedy sampling over a vocabulary shard: for every token, the largest
+ * logit of x_hat W^T over rows 0 .. vocab_local-1 and its vocabulary index
+ * (vocab_offset + row) are folded into argmax_keys[t] (atomic max of an
+ * orderable 64-bit key: higher logit first, then the lower index, as
+ * torch.argmax picks the first maximum).  argmax_keys must hold 0 (empty)
+ * before the first shard; krt_greedy_step reads and clears them. */
+typedef struct krt_lm_head_args {
+  const void* x;          /* bf16 [num_tokens, d_model], row stride x_stride */
+  const void* rms_weight; /* bf16 [d_model] (the final norm) */
+  const void* weight;     /* bf16 [vocab_local, d_model] this rank's lm_head rows */
+  unsigned long long* argmax_keys; /* [num_tokens] */
+  int32_t num_tokens, d_model, vocab_local, vocab_offset, x_stride;
+  float eps;
+  void* workspace;
+  size_t workspace_bytes;
+} krt_lm_head_args;
+KRT_API int krt_lm_head_argmax(const krt_lm_head_args* args, void* stream);
+
+/* Greedy choice and next-step input (one launch): for every sequence the
+ * token with the largest logit over all ranks' vocabulary shards
+ * (argmax_keys of this rank, exchanged through the communicator's peer
+ * buffers; comm may be NULL for one GPU), written to tokens[] on every rank;
+ * argmax_keys are cleared; the chosen token's embedding row is copied into
+ * hidden (when embedding is given) and positions / seq_lens, when given, are
+ * incremented.  Peer waits are bounded (status bit 16); a token outside the
+ * vocabulary sets bit 8 and becomes 0.  Calls sharing a communicator must be
+ * made in the same order on every rank. */
+typedef struct krt_greedy_step_args {
+  unsigned long long* argmax_keys; /* [num_seqs] from krt_lm_head_argmax */
+  int32_t* tokens;                 /* [num_seqs] out */
+  const void* embedding;           /* bf16 [vocab, d_model] or NULL */
+  void* hidden;                    /* bf16 [num_seqs, hidden_stride] out */
+  int32_t* positions;              /* [num_seqs] or NULL */
+  int32_t* seq_lens;               /* [num_seqs] or NULL */
+  int32_t num_seqs, d_model, hidden_stride, vocab;
+  void* status;                    /* a workspace header (krt_read_status) */
+  const int32_t* next_input;       /* [num_seqs] or NULL: where >= 0, that token's embedding is
+                                      fed to the next step instead of the chosen one's (prompt
+                                      tokens); tokens[] still receives the choice */
+} krt_greedy_step_args;
+KRT_API int krt_greedy_step(krt_comm* comm, const krt_greedy_step_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -305,17 +305,17 @@ struct DecodeCfg {
 // portable cluster size) while every cluster of the grid can be resident at
 // once; box depth and stage count follow from the shared memory left beside
 // the split's receive area.  KRT_DECODE_SPLITS overrides the split factor.
-DecodeCfg decode_config(int heads, int num_kb, int n_pad) {
+DecodeCfg decode_config(int heads, int num_kb, int n_pad, bool whole_tiles = false) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int>, DecodeCfg> cache;
+  static std::map<std::tuple<int, int, int, int, int>, DecodeCfg> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, heads, num_kb, n_pad);
+  const auto key = std::make_tuple(dev, heads, num_kb, n_pad, whole_tiles ? 1 : 0);
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   int tile_m = env_int("KRT_DECODE_TILE_M", heads <= 12 && n_pad <= 128 ? 64 : 128);
-  if (tile_m != 64) tile_m = 128;
+  if (tile_m != 64 || whole_tiles) tile_m = 128;
   const int tiles = heads * (128 / tile_m);
   DecodeCfg cfg{tile_m, tiles, 1, 1, 1};
   const int forced = env_int("KRT_DECODE_SPLITS", 0);
@@ -438,6 +438,112 @@ extern "C" int krt_read_status(void* workspace, void* stream, int32_t* bits) {
     return set_error(KRT_ERR_DEVICE, "kernel status bits 0x%x", v);
   }
   return clear_error();
+}
+
+// --------------------------------------------- decode-shaped projections
+namespace {
+
+// RMSNorm prep + the swap-AB split-K projection kernel with a non-QKV
+// epilogue (p.epi), weight rows in 128-row tiles.
+int run_projection(PagedParams& p, const void* weight, int weight_rows, const char* name, cudaStream_t s) {
+  const int tiles = (weight_rows + 127) / 128;
+  const int num_kb = p.d_model / kBK;
+  const DecodeCfg cfg = decode_config(tiles, num_kb, p.n_pad, true);
+  p.kc = cfg.kc;
+  p.stages = cfg.stages;
+  p.splits = cfg.splits;
+  p.prefetch = env_int("KRT_L2_PREFETCH_STAGES", 0);
+  int cols = 32;
+  while (cols < p.n_pad) cols <<= 1;
+  p.tmem_cols = cols;
+  CUtensorMap tmap_w, tmap_x;
+  int rc = make_tmap_bf16_3d(&tmap_w, weight, (uint64_t)weight_rows, (uint64_t)p.d_model, (uint64_t)p.d_model, 128,
+                             (uint32_t)p.kc);
+  if (rc) return rc;
+  rc = make_tmap_bf16_3d(&tmap_x, p.xhat, (uint64_t)p.num_tokens, (uint64_t)p.d_model, (uint64_t)p.d_model,
+                         (uint32_t)p.n_pad, (uint32_t)p.kc);
+  if (rc) return rc;
+  cudaError_t e = launch_qkv_prep(p, s);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  e = launch_qkv_rope_decode(128, tmap_w, tmap_x, p, tiles, s);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return clear_error();
+}
+
+// Shared checks and parameters of the RMSNorm + projection calls.
+int projection_params(PagedParams& p, const char* name, const void* x, const void* gamma, const void* weight,
+                      int num_tokens, int d_model, int x_stride, float eps, void* workspace, size_t ws_bytes) {
+  if (!x || !gamma || !weight || !workspace) return set_error(KRT_ERR_INVALID, "%s: a required pointer is NULL", name);
+  if (num_tokens <= 0 || num_tokens > 256)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: num_tokens must be in 1..256", name);
+  if (d_model <= 0 || d_model % kBK != 0)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: d_model must be a positive multiple of 64", name);
+  if (x_stride < d_model || x_stride % 8 != 0)
+    return set_error(KRT_ERR_INVALID, "%s: x_stride must be >= d_model and a multiple of 8", name);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(gamma) & 15) ||
+      (reinterpret_cast<uintptr_t>(weight) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return set_error(KRT_ERR_INVALID, "%s: tensors must be 16-byte aligned", name);
+  const size_t need = ws_layout(num_tokens, d_model).total;
+  if (ws_bytes < need) return set_error(KRT_ERR_WORKSPACE, "%s: workspace of %zu bytes, %zu needed", name, ws_bytes, need);
+  std::memset(&p, 0, sizeof(p));
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.gamma = static_cast<const __nv_bfloat16*>(gamma);
+  p.num_tokens = num_tokens;
+  p.n_pad = (num_tokens + 15) / 16 * 16;
+  p.d_model = d_model;
+  p.x_stride = x_stride;
+  p.eps = eps;
+  char* ws = static_cast<char*>(workspace);
+  const WsLayout L = ws_layout(num_tokens, d_model);
+  p.status = reinterpret_cast<int*>(ws);
+  p.tok_pos = reinterpret_cast<int*>(ws + L.pos_off);
+  p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
+  p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
+  return KRT_OK;
+}
+
+}  // namespace
+
+extern "C" size_t krt_projection_workspace_size(int32_t num_tokens, int32_t d_model) {
+  if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0) return 0;
+  return ws_layout(num_tokens, d_model).total;
+}
+
+extern "C" int krt_gate_up_swiglu(const krt_gate_up_args* a, void* stream) {
+  const char* name = "krt_gate_up_swiglu";
+  if (!a) return set_error(KRT_ERR_INVALID, "%s: args is NULL", name);
+  PagedParams p;
+  int rc = projection_params(p, name, a->x, a->rms_weight, a->gate_up_weight, a->num_tokens, a->d_model, a->x_stride,
+                             a->eps, a->workspace, a->workspace_bytes);
+  if (rc) return rc;
+  if (!a->act) return set_error(KRT_ERR_INVALID, "%s: act is NULL", name);
+  if (a->inter_local <= 0 || a->inter_local % 64 != 0)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: inter_local must be a positive multiple of 64", name);
+  if (a->act_stride < a->inter_local || a->act_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(a->act) & 15))
+    return set_error(KRT_ERR_INVALID, "%s: act must be 16-byte aligned with a stride >= inter_local, multiple of 8",
+                     name);
+  p.epi = kEpiSwiglu;
+  p.act = static_cast<__nv_bfloat16*>(a->act);
+  p.act_stride = a->act_stride;
+  return run_projection(p, a->gate_up_weight, 2 * a->inter_local, name, (cudaStream_t)stream);
+}
+
+extern "C" int krt_lm_head_argmax(const krt_lm_head_args* a, void* stream) {
+  const char* name = "krt_lm_head_argmax";
+  if (!a) return set_error(KRT_ERR_INVALID, "%s: args is NULL", name);
+  PagedParams p;
+  int rc = projection_params(p, name, a->x, a->rms_weight, a->weight, a->num_tokens, a->d_model, a->x_stride, a->eps,
+                             a->workspace, a->workspace_bytes);
+  if (rc) return rc;
+  if (!a->argmax_keys || (reinterpret_cast<uintptr_t>(a->argmax_keys) & 7))
+    return set_error(KRT_ERR_INVALID, "%s: argmax_keys must be an 8-byte aligned buffer", name);
+  if (a->vocab_local <= 0 || a->vocab_offset < 0)
+    return set_error(KRT_ERR_INVALID, "%s: vocab_local must be positive and vocab_offset >= 0", name);
+  p.epi = kEpiArgmax;
+  p.keys = a->argmax_keys;
+  p.vocab_valid = a->vocab_local;
+  p.vocab_offset = a->vocab_offset;
+  return run_projection(p, a->weight, a->vocab_local, name, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------------------ prefill

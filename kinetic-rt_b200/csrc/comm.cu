@@ -147,6 +147,98 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const T* __restri
   }
 }
 
+// ------------------------------------------------------ greedy sampling
+struct GreedyParams {
+  unsigned long long* keys;
+  int32_t* tokens;
+  const __nv_bfloat16* embedding;
+  __nv_bfloat16* hidden;
+  int32_t* positions;
+  int32_t* seq_lens;
+  const int32_t* next_input;
+  int* status;
+  int num_seqs, d_model, hidden_stride, vocab;
+};
+
+// 49-bit form of a (logit, index) key for the flagged exchange: the
+// orderable logit bits above a 17-bit inverted index (vocabularies below
+// 2^17 entries); 0 stays 0 (no entry).
+__device__ __forceinline__ uint64_t key49(unsigned long long key) {
+  if (key == 0ull) return 0ull;
+  const uint32_t idx = argmax_key_index(key);
+  return ((uint64_t)(key >> 32) << 17) | (uint64_t)(0x1FFFFu - (idx & 0x1FFFFu));
+}
+
+// One CTA per sequence: the chosen token (max over ranks' keys), then its
+// embedding row into the hidden state of the next step.
+__global__ void __launch_bounds__(128) greedy_step_kernel(const GreedyParams g, const CommView cv) {
+  pdl_wait();  // the keys come from the lm_head kernel
+  pdl_launch_dependents();
+  __shared__ int tok_s;
+  const int b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const unsigned long long key = g.keys[b];
+    g.keys[b] = 0ull;  // empty for the next lm_head call
+    int tok = 0;
+    bool have = key != 0ull;
+    if (cv.world == 1) {
+      if (have) tok = (int)argmax_key_index(key);
+    } else {
+      uint32_t* ep = reinterpret_cast<uint32_t*>(cv.base[cv.rank] + cv.L.greedy_epoch_off) + b;
+      uint32_t e = *ep + 1u;
+      if (e > 32767u) e = 1u;
+      *ep = e;
+      const uint64_t word = ((uint64_t)e << 49) | key49(key);
+      const size_t slot = ((size_t)(e & 1u) * kMaxWorld + cv.rank) * kMaxGreedySeqs + b;
+      for (int q = 0; q < cv.world; ++q) {
+        uint64_t* dst = reinterpret_cast<uint64_t*>(cv.base[q] + cv.L.greedy_off) + slot;
+        asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(word) : "memory");
+      }
+      uint64_t best = 0ull;
+      const uint64_t t0 = globaltimer_ns();
+      bool ok = true;
+      for (int q = 0; q < cv.world && ok; ++q) {
+        const uint64_t* src = reinterpret_cast<const uint64_t*>(cv.base[cv.rank] + cv.L.greedy_off) +
+                              ((size_t)(e & 1u) * kMaxWorld + q) * kMaxGreedySeqs + b;
+        while (true) {
+          uint64_t w;
+          asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
+          if ((uint32_t)(w >> 49) == e) {
+            const uint64_t k = w & ((1ull << 49) - 1ull);
+            best = k > best ? k : best;
+            break;
+          }
+          if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (!ok) atomicOr(g.status, kStatusTimeoutPeer);
+      have = ok && best != 0ull;
+      if (have) tok = (int)(0x1FFFFu - (uint32_t)(best & 0x1FFFFu));
+    }
+    if (tok < 0 || tok >= g.vocab) {
+      atomicOr(g.status, kStatusBadBlock);
+      tok = 0;
+    }
+    g.tokens[b] = tok;
+    if (g.next_input) {
+      const int forced = g.next_input[b];
+      if (forced >= 0 && forced < g.vocab) tok = forced;
+    }
+    tok_s = tok;
+    if (g.positions) g.positions[b] += 1;
+    if (g.seq_lens) g.seq_lens[b] += 1;
+  }
+  __syncthreads();
+  if (g.embedding) {
+    const uint4* src = reinterpret_cast<const uint4*>(g.embedding + (size_t)tok_s * g.d_model);
+    uint4* dst = reinterpret_cast<uint4*>(g.hidden + (size_t)b * g.hidden_stride);
+    for (int v = threadIdx.x; v < g.d_model / 8; v += blockDim.x) dst[v] = src[v];
+  }
+}
+
 }  // namespace krt
 
 using namespace krt;
@@ -387,6 +479,8 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
   p.k_local = a->k_local;
   p.y_stride = a->y_stride;
   p.status = static_cast<int*>(a->workspace);
+  if (a->residual && (reinterpret_cast<uintptr_t>(a->residual) & 15))
+    return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: residual must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   for (int t0 = 0; t0 < a->num_tokens; t0 += 256) {
     const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
@@ -404,6 +498,7 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     while (cols < p.n_pad) cols <<= 1;
     p.tmem_cols = cols;
     p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
+    p.residual = a->residual ? static_cast<const __nv_bfloat16*>(a->residual) + (size_t)t0 * a->y_stride : nullptr;
     const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
     CUtensorMap tmap_w, tmap_x;
     int rc = make_tmap_bf16_3d(&tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local, (uint64_t)a->k_local,
@@ -415,5 +510,56 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     cudaError_t e = launch_rowparallel_gemm_ar(cfg.tile_m, tmap_w, tmap_x, p, cfg.tiles, s);
     if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
   }
+  return clear_error();
+}
+
+// ------------------------------------------------------ greedy sampling
+extern "C" int krt_greedy_step(krt_comm* c, const krt_greedy_step_args* a, void* stream) {
+  const char* name = "krt_greedy_step";
+  if (!a) return set_error(KRT_ERR_INVALID, "%s: args is NULL", name);
+  if (!a->argmax_keys || !a->tokens || !a->status) return set_error(KRT_ERR_INVALID, "%s: NULL buffer", name);
+  if (a->num_seqs <= 0 || a->num_seqs > kMaxGreedySeqs)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: num_seqs must be in 1..%d", name, kMaxGreedySeqs);
+  if (a->vocab <= 0 || a->vocab > (1 << 17))
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: vocab must be in 1..131072", name);
+  if (a->embedding) {
+    if (!a->hidden) return set_error(KRT_ERR_INVALID, "%s: hidden is NULL", name);
+    if (a->d_model <= 0 || a->d_model % 8 != 0 || a->hidden_stride < a->d_model || a->hidden_stride % 8 != 0 ||
+        (reinterpret_cast<uintptr_t>(a->embedding) & 15) || (reinterpret_cast<uintptr_t>(a->hidden) & 15))
+      return set_error(KRT_ERR_INVALID, "%s: embedding rows and hidden must be 16-byte aligned, d_model % 8 == 0",
+                       name);
+  }
+  GreedyParams g;
+  g.keys = a->argmax_keys;
+  g.tokens = a->tokens;
+  g.embedding = static_cast<const __nv_bfloat16*>(a->embedding);
+  g.hidden = static_cast<__nv_bfloat16*>(a->hidden);
+  g.positions = a->positions;
+  g.seq_lens = a->seq_lens;
+  g.next_input = a->next_input;
+  g.status = static_cast<int*>(a->status);
+  g.num_seqs = a->num_seqs;
+  g.d_model = a->d_model;
+  g.hidden_stride = a->hidden_stride;
+  g.vocab = a->vocab;
+  CommView v;
+  if (c) {
+    int rc = comm_view(c, &v);
+    if (rc) return rc;
+  } else {
+    std::memset(&v, 0, sizeof(v));
+    v.world = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a->num_seqs, 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, greedy_step_kernel, g, v);
+  if (e != cudaSuccess) return cuda_error(e, name);
   return clear_error();
 }

@@ -16,6 +16,7 @@ namespace krt {
 constexpr int kMaxWorld = 8;
 constexpr int kArMaxCtas = 64;     // CTAs of the standalone allreduce
 constexpr int kMaxChunks = 16;     // 256 tokens per launch
+constexpr int kMaxGreedySeqs = 1024;  // sequences per krt_greedy_step call
 
 struct CommLayout {
   int world, max_n, tiles;
@@ -44,6 +45,11 @@ struct CommLayout {
   size_t ll_stage_off[2];   // [world (source)][stage tiles][kMaxChunks][rows/32 pairs][128 threads]
   size_t ll_result_off[2];  // [tiles][kMaxChunks][rows/32 pairs][128 threads]
   size_t epoch_off[2];      // u32 [tiles][kMaxChunks] uses of each (tile, chunk), cycling 1..65534
+  // Greedy sampling across vocabulary shards: per sequence one flagged word
+  // (15-bit epoch << 49 | 49-bit (logit, index) key) from every rank, in
+  // two copies alternating by epoch parity; per-sequence epoch counters.
+  size_t greedy_off;        // u64 [2][kMaxWorld (source)][kMaxGreedySeqs]
+  size_t greedy_epoch_off;  // u32 [kMaxGreedySeqs]
   int owned_tiles[2];       // ceil(tiles / world): tile t is reduced by rank t % world
   int stage_tiles[2];       // tile slots per source: 2 x all tiles (world 2) or the owned ones
   size_t total;
@@ -73,6 +79,9 @@ inline CommLayout comm_layout(int world, int max_n) {
     L.epoch_off[v] = up(L.ll_result_off[v] + (size_t)tiles * kMaxChunks * slot);
     off = up(L.epoch_off[v] + (size_t)tiles * kMaxChunks * 4);
   }
+  L.greedy_off = off;
+  L.greedy_epoch_off = up(off + (size_t)2 * kMaxWorld * kMaxGreedySeqs * 8);
+  off = up(L.greedy_epoch_off + (size_t)kMaxGreedySeqs * 4);
   L.total = off;
   return L;
 }
@@ -87,6 +96,7 @@ struct CommView {
 // Launch parameters of the fused row-parallel GEMM + allreduce (gemm_ar.cu).
 struct GemmArParams {
   __nv_bfloat16* y;
+  const __nv_bfloat16* residual;  // optional: y = residual + sum (same strides as y; may be y itself)
   int y_stride;
   int num_tokens, n_pad, n_out, k_local;
   int splits, stages, kc, tmem_cols;

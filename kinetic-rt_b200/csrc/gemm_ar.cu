@@ -111,6 +111,23 @@ __device__ __forceinline__ void store_bf16_rows(__nv_bfloat16* dst, const uint32
     reinterpret_cast<uint4*>(dst)[h] = make_uint4(w[4 * h], w[4 * h + 1], w[4 * h + 2], w[4 * h + 3]);
 }
 
+// acc[i] += residual[i] for RG bf16 values (16-byte loads); no-op without a residual.
+template <int RG>
+__device__ __forceinline__ void add_residual_rows(float* acc, const __nv_bfloat16* res) {
+  if (res == nullptr) return;
+#pragma unroll
+  for (int h = 0; h < RG / 8; ++h) {
+    const uint4 v = reinterpret_cast<const uint4*>(res)[h];
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(b2[q]);
+      acc[8 * h + 2 * q] += f.x;
+      acc[8 * h + 2 * q + 1] += f.y;
+    }
+  }
+}
+
 template <int TM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     rowparallel_gemm_ar_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
@@ -349,6 +366,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (world == 1) {
         if (alive && t < T) {
+          add_residual_rows<RG>(y, p.residual ? p.residual + (size_t)t * p.y_stride + row0 + RG * g : nullptr);
           uint32_t w[RG / 2];
 #pragma unroll
           for (int i = 0; i < RG / 2; ++i) w[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
@@ -395,6 +413,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
           if (!ok || t >= T) continue;
+          add_residual_rows<RG>(acc, p.residual ? p.residual + (size_t)t * p.y_stride + row0 + RG * g : nullptr);
           uint32_t w[RG / 2];
 #pragma unroll
           for (int i = 0; i < RG / 2; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);

@@ -49,8 +49,13 @@ struct DecodeSmemTail {
   uint64_t recv;  // completes when the other ranks' partials of the owned chunks have arrived
   uint32_t tmem_base;
   int abort;
-  int pos[256];
-  long long slot[256];
+  union {
+    struct {
+      int pos[256];
+      long long slot[256];
+    };                            // kEpiQkv: per-token position and pool slot
+    unsigned long long key[256];  // kEpiArgmax: the CTA's best (logit, index) per token
+  };
 };
 
 // Pipeline buffers; after the main loop they hold the parked partial.
@@ -86,7 +91,7 @@ __device__ __forceinline__ int head_row(int i, int half) {
   return i < 32 ? 32 * half + i : 64 + 32 * half + (i - 32);
 }
 
-template <int TM>
+template <int TM, int EPI>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     qkv_rope_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                            const PagedParams p) {
@@ -232,15 +237,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     const int j = ept & 15, g = ept >> 4, gp = g ^ 4;
     const int hr0 = head_row<TM>(RG * g, half), hrp0 = head_row<TM>(RG * gp, half);
     const float sign = g < 4 ? -1.f : 1.f;
-    const bool rot = head < p.n_heads + p.n_kv_heads;
+    // rows whose rotate-half / gate-up partner rows are summed as well
+    const bool rot = EPI == kEpiQkv ? head < p.n_heads + p.n_kv_heads : (EPI == kEpiSwiglu ? g < 4 : false);
     const int rank = split;  // cluster (1, splits, 1): rank == blockIdx.y
     const int nranks = p.splits;
     pdl_wait();
-    for (int t = ept; t < T; t += 128) {
-      tl->pos[t] = p.tok_pos[t];
-      tl->slot[t] = p.tok_slot[t];
+    if (EPI == kEpiQkv) {
+      for (int t = ept; t < T; t += 128) {
+        tl->pos[t] = p.tok_pos[t];
+        tl->slot[t] = p.tok_slot[t];
+      }
+    } else if (EPI == kEpiArgmax) {
+      for (int t = ept; t < n_pad; t += 128) tl->key[t] = 0ull;
     }
-    {
+    if (EPI == kEpiQkv) {
       const int t0 = rank * 16 + j;
       if (t0 < T && rot) load_rope_n<RG>(p, p.tok_pos[t0], hr0, cs0, sn0);
 #pragma unroll
@@ -248,6 +258,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         bias_y[i] = p.bias ? __bfloat162float(p.bias[head * kHeadDim + hr0 + i]) : 0.f;
         bias_p[i] = p.bias ? __bfloat162float(p.bias[head * kHeadDim + hrp0 + i]) : 0.f;
       }
+    } else {
+#pragma unroll
+      for (int i = 0; i < RG; ++i) bias_y[i] = bias_p[i] = 0.f;
     }
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
     if (!waited && lane == 0) decode_fail(p, tl, kStatusTimeoutAccum);
@@ -308,9 +321,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       for (int c = rank; c * 16 < T; c += nranks) {
         const int t = c * 16 + j;
         if (t >= T) continue;
-        const int pos = tl->pos[t];
+        if (EPI == kEpiSwiglu && g >= 4) continue;  // up rows: read as partners of the gate rows
+        const int pos = EPI == kEpiQkv ? tl->pos[t] : 0;
         float4 cs[RG / 4], sn[RG / 4];
-        if (rot) {
+        if (EPI == kEpiQkv && rot) {
           if (c == rank) {
 #pragma unroll
             for (int k4 = 0; k4 < RG / 4; ++k4) {
@@ -352,8 +366,39 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             if (rot) add_f4<RG>(yp, b[qq]);
           }
         }
-        store_rows_n<RG>(p, head, t, hr0, sign, pos, tl->slot[t], y, yp, cs, sn);
+        if (EPI == kEpiQkv) {
+          store_rows_n<RG>(p, head, t, hr0, sign, pos, tl->slot[t], y, yp, cs, sn);
+        } else if (EPI == kEpiSwiglu) {
+          // features tile * 64 + RG * g .. +RG-1: silu(gate) * up
+          uint32_t w[RG / 2];
+#pragma unroll
+          for (int i = 0; i < RG / 2; ++i) {
+            const float a0 = y[2 * i] / (1.f + __expf(-y[2 * i])) * yp[2 * i];
+            const float a1 = y[2 * i + 1] / (1.f + __expf(-y[2 * i + 1])) * yp[2 * i + 1];
+            w[i] = pack_bf16x2(a0, a1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(p.act + (size_t)t * p.act_stride + (size_t)tile * 64 + RG * g);
+#pragma unroll
+          for (int h = 0; h < RG / 8; ++h) dst[h] = make_uint4(w[4 * h], w[4 * h + 1], w[4 * h + 2], w[4 * h + 3]);
+        } else {
+          // vocabulary rows tile * 128 + RG * g + i
+          unsigned long long best = 0ull;
+#pragma unroll
+          for (int i = 0; i < RG; ++i) {
+            const int row = tile * 128 + RG * g + i;
+            if (row < p.vocab_valid) {
+              const unsigned long long k = argmax_key(y[i], (uint32_t)(p.vocab_offset + row));
+              best = k > best ? k : best;
+            }
+          }
+          atomicMax(&tl->key[t], best);
+        }
       }
+    }
+    if (EPI == kEpiArgmax) {
+      named_bar_sync(1, 128);
+      for (int t = ept; t < T; t += 128)
+        if (tl->key[t] != 0ull) atomicMax(p.keys + t, tl->key[t]);
     }
     if ((ept & 31) == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }
@@ -378,12 +423,12 @@ size_t decode_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits) 
                       : decode_smem_bytes_t<128>(stages, n_pad, kc, splits);
 }
 
-template <int TM>
+template <int TM, int EPI>
 static cudaError_t launch_decode_t(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                    int tiles, cudaStream_t stream) {
   const size_t smem = decode_smem_bytes_t<TM>(p.stages, p.n_pad, p.kc, p.splits);
   cudaError_t e =
-      cudaFuncSetAttribute(qkv_rope_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(qkv_rope_decode_kernel<TM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, p.splits, 1);
@@ -399,20 +444,22 @@ static cudaError_t launch_decode_t(const CUtensorMap& tmap_w, const CUtensorMap&
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, qkv_rope_decode_kernel<TM>, tmap_w, tmap_x, p);
+  return cudaLaunchKernelEx(&cfg, qkv_rope_decode_kernel<TM, EPI>, tmap_w, tmap_x, p);
 }
 
 cudaError_t launch_qkv_rope_decode(int tile_m, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
                                    const PagedParams& p, int tiles, cudaStream_t stream) {
-  return tile_m == 64 ? launch_decode_t<64>(tmap_w, tmap_x, p, tiles, stream)
-                      : launch_decode_t<128>(tmap_w, tmap_x, p, tiles, stream);
+  if (p.epi == kEpiSwiglu) return launch_decode_t<128, kEpiSwiglu>(tmap_w, tmap_x, p, tiles, stream);
+  if (p.epi == kEpiArgmax) return launch_decode_t<128, kEpiArgmax>(tmap_w, tmap_x, p, tiles, stream);
+  return tile_m == 64 ? launch_decode_t<64, kEpiQkv>(tmap_w, tmap_x, p, tiles, stream)
+                      : launch_decode_t<128, kEpiQkv>(tmap_w, tmap_x, p, tiles, stream);
 }
 
 // Largest cluster count that can be resident at once for a given split.
 template <int TM>
 static int decode_max_active_clusters_t(int splits, int n_pad, int stages, int kc) {
   const size_t smem = decode_smem_bytes_t<TM>(stages, n_pad, kc, splits);
-  if (cudaFuncSetAttribute(qkv_rope_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (cudaFuncSetAttribute(qkv_rope_decode_kernel<TM, kEpiQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return 0;
   cudaLaunchConfig_t cfg = {};
@@ -427,7 +474,7 @@ static int decode_max_active_clusters_t(int splits, int n_pad, int stages, int k
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, qkv_rope_decode_kernel<TM>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, qkv_rope_decode_kernel<TM, kEpiQkv>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }

@@ -3,6 +3,7 @@
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda.h>
+#include <cstring>
 
 #include "ptx.cuh"
 
@@ -42,7 +43,40 @@ struct PagedParams {
   int* tok_pos;       // [num_tokens] position, or -1 when outside the RoPE table
   long long* tok_slot;  // [num_tokens] pool slot, or -1 when the block lookup failed
   __nv_bfloat16* xhat;  // [num_tokens, d_model] bf16(x * rsqrt(mean(x^2)+eps) * gamma)
+  // Epilogue of the decode kernel (kEpi*); the fields below serve the
+  // non-QKV epilogues.
+  int epi;
+  __nv_bfloat16* act;   // kEpiSwiglu: [num_tokens, act_stride] silu(gate) * up
+  int act_stride;
+  unsigned long long* keys;  // kEpiArgmax: [num_tokens] packed (logit, index) maxima
+  int vocab_valid;      // kEpiArgmax: weight rows that are real vocabulary entries
+  int vocab_offset;     // kEpiArgmax: vocabulary index of weight row 0
 };
+
+// Epilogues of the decode-shaped (swap-AB, split-K) projection kernel:
+//   kEpiQkv     bias, RoPE, Q out, K/V scattered into the paged pool
+//   kEpiSwiglu  weight rows in 64-row groups [gate f..f+63 | up f..f+63]:
+//               act[t, f + i] = silu(gate) * up
+//   kEpiArgmax  logits of a vocabulary shard: per token the largest logit
+//               and its index, folded into keys[t] with atomicMax
+enum : int { kEpiQkv = 0, kEpiSwiglu = 1, kEpiArgmax = 2 };
+
+// Orderable 64-bit key of (logit, vocabulary index): larger logits give
+// larger keys, and for equal logits the smaller index gives the larger key
+// (the first maximum, as torch.argmax returns it).
+__host__ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  uint32_t u;
+#ifdef __CUDA_ARCH__
+  u = __float_as_uint(v);
+#else
+  memcpy(&u, &v, 4);
+#endif
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+__host__ __device__ __forceinline__ uint32_t argmax_key_index(unsigned long long key) {
+  return 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
+}
 
 // Workspace layout shared by the decode and prefill paths.
 struct WsLayout {

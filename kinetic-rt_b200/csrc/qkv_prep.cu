@@ -55,8 +55,9 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(const PagedParam
   const int t = blockIdx.x;
   if (t >= p.num_tokens) return;
   if (threadIdx.x >= 128) {
-    // Warp 4: the slot lookup, whose dependent loads overlap the RMS pass.
-    if (threadIdx.x == 128) {
+    // Warp 4: the slot lookup, whose dependent loads overlap the RMS pass
+    // (only the QKV projection has positions and pool slots).
+    if (threadIdx.x == 128 && p.positions != nullptr) {
       const int pos = p.positions[t];
       const bool pos_ok = pos >= 0 && pos < p.max_position;
       const long long sl = token_slot(p, t);

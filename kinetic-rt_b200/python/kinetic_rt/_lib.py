@@ -58,7 +58,7 @@ class GemmArArgs(ctypes.Structure):
     _fields_ = [
         ("x", _vp), ("weight", _vp), ("y", _vp),
         ("num_tokens", _i32), ("k_local", _i32), ("n_out", _i32), ("x_stride", _i32), ("y_stride", _i32),
-        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("residual", _vp),
     ]
 
 
@@ -71,6 +71,34 @@ class PagedAttentionArgs(ctypes.Structure):
         ("block_table_stride", _i32), ("num_blocks", _i32), ("tokens_per_block", _i32),
         ("max_seq_len", _i32), ("scale", ctypes.c_float),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class GateUpArgs(ctypes.Structure):
+    """krt_gate_up_args"""
+    _fields_ = [
+        ("x", _vp), ("rms_weight", _vp), ("gate_up_weight", _vp), ("act", _vp),
+        ("num_tokens", _i32), ("d_model", _i32), ("inter_local", _i32), ("x_stride", _i32), ("act_stride", _i32),
+        ("eps", ctypes.c_float), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class LmHeadArgs(ctypes.Structure):
+    """krt_lm_head_args"""
+    _fields_ = [
+        ("x", _vp), ("rms_weight", _vp), ("weight", _vp), ("argmax_keys", _vp),
+        ("num_tokens", _i32), ("d_model", _i32), ("vocab_local", _i32), ("vocab_offset", _i32), ("x_stride", _i32),
+        ("eps", ctypes.c_float), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class GreedyStepArgs(ctypes.Structure):
+    """krt_greedy_step_args"""
+    _fields_ = [
+        ("argmax_keys", _vp), ("tokens", _vp), ("embedding", _vp), ("hidden", _vp),
+        ("positions", _vp), ("seq_lens", _vp),
+        ("num_seqs", _i32), ("d_model", _i32), ("hidden_stride", _i32), ("vocab", _i32),
+        ("status", _vp), ("next_input", _vp),
     ]
 
 
@@ -95,6 +123,10 @@ SIGNATURES = {
     "krt_rowparallel_gemm_ar": (ctypes.c_int, [_vp, ctypes.POINTER(GemmArArgs), _vp]),
     "krt_paged_attention_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "krt_paged_attention_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttentionArgs), _vp]),
+    "krt_projection_workspace_size": (ctypes.c_size_t, [_i32, _i32]),
+    "krt_gate_up_swiglu": (ctypes.c_int, [ctypes.POINTER(GateUpArgs), _vp]),
+    "krt_lm_head_argmax": (ctypes.c_int, [ctypes.POINTER(LmHeadArgs), _vp]),
+    "krt_greedy_step": (ctypes.c_int, [_vp, ctypes.POINTER(GreedyStepArgs), _vp]),
 }
 
 _lib = None
@@ -249,8 +281,11 @@ def gemm_ar_workspace_bytes():
     return int(lib().krt_rowparallel_gemm_ar_workspace_size())
 
 
-def gemm_ar_args(x, weight, y, workspace):
+def gemm_ar_args(x, weight, y, workspace, residual=None):
+    """residual: optional bf16 tensor with y's row stride (may be y itself):
+    y = residual + allreduce(x @ weight^T)."""
     a = GemmArArgs()
+    a.residual = _ptr(residual)
     a.x, a.weight, a.y = _ptr(x), _ptr(weight), _ptr(y)
     a.num_tokens, a.k_local = int(x.shape[0]), int(x.shape[1])
     a.n_out = int(weight.shape[0])
@@ -286,3 +321,75 @@ def attention_args(q, kv_pool, block_table, seq_lens, out, n_heads, n_kv_heads, 
 
 def paged_attention_decode(args, stream=None):
     check(lib().krt_paged_attention_decode(ctypes.byref(args), _stream(stream)))
+
+
+# ------------------------------------------------- rest of the decode step
+def projection_workspace_bytes(num_tokens, d_model):
+    return int(lib().krt_projection_workspace_size(num_tokens, d_model))
+
+
+def gate_up_args(x, rms_weight, gate_up_weight, act, workspace, eps=1e-5):
+    """gate_up_weight: bf16 [2 * inter_local, d_model] in 64-row [gate | up] groups
+    (interleave_gate_up)."""
+    a = GateUpArgs()
+    a.x, a.rms_weight, a.gate_up_weight, a.act = _ptr(x), _ptr(rms_weight), _ptr(gate_up_weight), _ptr(act)
+    a.num_tokens, a.d_model = int(x.shape[0]), int(x.shape[1])
+    a.inter_local = int(gate_up_weight.shape[0]) // 2
+    a.x_stride, a.act_stride = int(x.stride(0)), int(act.stride(0))
+    a.eps = float(eps)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel() * workspace.element_size()
+    return a
+
+
+def gate_up_swiglu(args, stream=None):
+    check(lib().krt_gate_up_swiglu(ctypes.byref(args), _stream(stream)))
+
+
+def interleave_gate_up(gate, up):
+    """[inter, d] gate and up shards -> [2 * inter, d] in 64-row [gate | up] groups."""
+    inter, d = gate.shape
+    assert inter % 64 == 0 and up.shape == gate.shape
+    return __import__("torch").stack([gate.view(inter // 64, 64, d), up.view(inter // 64, 64, d)], 1).reshape(
+        2 * inter, d)
+
+
+def lm_head_args(x, rms_weight, weight, keys, workspace, vocab_offset=0, eps=1e-5):
+    a = LmHeadArgs()
+    a.x, a.rms_weight, a.weight, a.argmax_keys = _ptr(x), _ptr(rms_weight), _ptr(weight), _ptr(keys)
+    a.num_tokens, a.d_model = int(x.shape[0]), int(x.shape[1])
+    a.vocab_local, a.vocab_offset = int(weight.shape[0]), int(vocab_offset)
+    a.x_stride = int(x.stride(0))
+    a.eps = float(eps)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel() * workspace.element_size()
+    return a
+
+
+def lm_head_argmax(args, stream=None):
+    check(lib().krt_lm_head_argmax(ctypes.byref(args), _stream(stream)))
+
+
+def greedy_step_args(keys, tokens, status, vocab, embedding=None, hidden=None, positions=None, seq_lens=None,
+                     next_input=None):
+    a = GreedyStepArgs()
+    a.next_input = _ptr(next_input)
+    a.argmax_keys, a.tokens, a.status = _ptr(keys), _ptr(tokens), _ptr(status)
+    a.embedding, a.hidden, a.positions, a.seq_lens = _ptr(embedding), _ptr(hidden), _ptr(positions), _ptr(seq_lens)
+    a.num_seqs = int(tokens.shape[0])
+    a.d_model = 0 if embedding is None else int(embedding.shape[1])
+    a.hidden_stride = 0 if hidden is None else int(hidden.stride(0))
+    a.vocab = int(vocab)
+    return a
+
+
+def greedy_step(comm, args, stream=None):
+    check(lib().krt_greedy_step(comm, ctypes.byref(args), _stream(stream)))
+
+
+def argmax_key(value, index):
+    """Host form of the (logit, index) key the kernels fold with atomicMax."""
+    import struct
+    u = struct.unpack("<I", struct.pack("<f", float(value)))[0]
+    u = (~u & 0xFFFFFFFF) if u & 0x80000000 else (u | 0x80000000)
+    return (u << 32) | (0xFFFFFFFF - int(index))

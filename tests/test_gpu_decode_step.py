@@ -1,0 +1,184 @@
+"""GPU parity of the decode-step pieces around the hot path and of a whole
+decode step (tiny Llama-shaped stack) against oracle/decoder.py.
+
+bf16 tolerance: max-abs 2e-2 + rel 1e-2 (per element, as the other GPU
+tests); greedy tokens must match the oracle's argmax unless the oracle's
+top two logits are within that tolerance of each other (a near-tie that
+bf16 rounding may order either way).
+"""
+import numpy as np
+import pytest
+
+from oracle import decoder as odec
+from oracle import fused_layer
+from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits, round_bf16
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-2, 1e-2
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def bf(rng, *shape, scale=1.0, base=0.0):
+    return round_bf16((rng.standard_normal(shape, dtype=np.float32) * np.float32(scale) + np.float32(base)))
+
+
+def dev(torch, a):
+    return torch.from_numpy(f32_to_bf16_bits(a).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def test_gate_up_swiglu(torch_cuda):
+    torch = torch_cuda
+    from python.kinetic_rt import _lib
+    rng = np.random.Generator(np.random.PCG64(1))
+    T, D, I = 37, 512, 320
+    x, g = bf(rng, T, D), bf(rng, D, scale=0.1, base=1.0)
+    wg, wu = bf(rng, I, D, scale=0.05), bf(rng, I, D, scale=0.05)
+    act = torch.full((T, I + 16), 5.0, dtype=torch.bfloat16, device="cuda")[:, :I]
+    ws = torch.zeros(_lib.projection_workspace_bytes(T, D), dtype=torch.uint8, device="cuda")
+    wgu = _lib.interleave_gate_up(dev(torch, wg), dev(torch, wu)).contiguous()
+    _lib.gate_up_swiglu(_lib.gate_up_args(dev(torch, x), dev(torch, g), wgu, act, ws))
+    assert _lib.read_status(ws) == (0, 0)
+    xm = round_bf16(fused_layer.rms_norm(x, g)).astype(np.float64)
+    gg, uu = xm @ wg.astype(np.float64).T, xm @ wu.astype(np.float64).T
+    ref = odec.silu(gg) * uu
+    np.testing.assert_allclose(act.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+
+
+def _check_argmax(logits, idx):
+    best = logits.max(-1)
+    chosen = logits[np.arange(len(idx)), idx]
+    assert np.all(chosen >= best - (ATOL + RTOL * np.abs(best))), (chosen, best)
+    return np.mean(idx == logits.argmax(-1))
+
+
+def test_lm_head_argmax_two_shards(torch_cuda):
+    """Two vocabulary shards (1000 + 777 rows, neither a multiple of 128) folded
+    into one key array give the argmax over the whole vocabulary."""
+    torch = torch_cuda
+    from python.kinetic_rt import _lib
+    rng = np.random.Generator(np.random.PCG64(2))
+    T, D, V0, V1 = 19, 256, 1000, 777
+    x, g = bf(rng, T, D), bf(rng, D, scale=0.1, base=1.0)
+    w = bf(rng, V0 + V1, D, scale=0.05)
+    keys = torch.zeros(T, dtype=torch.int64, device="cuda")
+    ws = torch.zeros(_lib.projection_workspace_bytes(T, D), dtype=torch.uint8, device="cuda")
+    wd = dev(torch, w)
+    for lo, hi in ((0, V0), (V0, V0 + V1)):
+        _lib.lm_head_argmax(_lib.lm_head_args(dev(torch, x), dev(torch, g), wd[lo:hi], keys, ws, vocab_offset=lo))
+    assert _lib.read_status(ws) == (0, 0)
+    k = keys.cpu().numpy().view(np.uint64)
+    idx = (0xFFFFFFFF - (k & np.uint64(0xFFFFFFFF))).astype(np.int64)
+    xm = round_bf16(fused_layer.rms_norm(x, g)).astype(np.float64)
+    logits = xm @ w.astype(np.float64).T
+    assert _check_argmax(logits, idx) > 0.9
+    # the key carries the fp32 logit of the chosen row
+    vals = ((k >> np.uint64(32)).astype(np.uint32))
+    vals = np.where(vals & 0x80000000, vals & 0x7FFFFFFF, ~vals & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+    np.testing.assert_allclose(vals, logits[np.arange(T), idx], atol=ATOL, rtol=RTOL)
+
+
+def test_greedy_step_single_gpu(torch_cuda):
+    torch = torch_cuda
+    from python.kinetic_rt import _lib
+    B, V, D = 6, 50, 64
+    vals = [0.5, -1.0, 3.25, 0.0, -0.0, 7.0]
+    idxs = [3, 49, 0, 17, 2, 11]
+    keys = torch.tensor([_lib.argmax_key(v, i) - (1 << 64 if _lib.argmax_key(v, i) >= 1 << 63 else 0)
+                         for v, i in zip(vals, idxs)], dtype=torch.int64, device="cuda")
+    tokens = torch.full((B,), -5, dtype=torch.int32, device="cuda")
+    emb = torch.randn(V, D, device="cuda").to(torch.bfloat16)
+    hidden = torch.zeros(B, D + 8, dtype=torch.bfloat16, device="cuda")
+    pos = torch.arange(B, dtype=torch.int32, device="cuda")
+    lens = pos + 1
+    forced = torch.tensor([-1, -1, 7, -1, -1, -1], dtype=torch.int32, device="cuda")
+    status = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    _lib.greedy_step(None, _lib.greedy_step_args(keys, tokens, status, V, emb, hidden, pos, lens, next_input=forced))
+    assert _lib.read_status(status) == (0, 0)
+    assert tokens.cpu().tolist() == idxs
+    fed = [7 if i == 2 else t for i, t in enumerate(idxs)]
+    assert torch.equal(hidden[:, :D], emb[torch.tensor(fed, device="cuda")])
+    assert pos.cpu().tolist() == list(range(1, B + 1)) and lens.cpu().tolist() == list(range(2, B + 2))
+    assert int(keys.abs().sum()) == 0
+
+
+def test_gemm_residual_in_place(torch_cuda):
+    torch = torch_cuda
+    from python.kinetic_rt import _lib
+    rng = np.random.Generator(np.random.PCG64(3))
+    T, K, N = 21, 640, 384
+    x, w, h = bf(rng, T, K), bf(rng, N, K, scale=0.02), bf(rng, T, N)
+    hd = dev(torch, h)
+    ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    _lib.rowparallel_gemm_ar(None, _lib.gemm_ar_args(dev(torch, x), dev(torch, w), hd, ws, residual=hd))
+    assert _lib.read_status(ws) == (0, 0)
+    ref = h.astype(np.float64) + x.astype(np.float64) @ w.astype(np.float64).T
+    np.testing.assert_allclose(hd.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+
+
+def tiny_model(rng, L=2, D=256, H=4, KV=2, I=384, V=1000):
+    from python.kinetic_rt.decoder import LlamaShape
+    shape = LlamaShape(n_layers=L, d_model=D, n_heads=H, n_kv_heads=KV, inter=I, vocab=V, rope_theta=1e4)
+    hd = 128
+    full = {k: [] for k in ("qkv", "g_attn", "o", "g_mlp", "gate", "up", "down")}
+    for _ in range(L):
+        full["qkv"].append(bf(rng, (H + 2 * KV) * hd, D, scale=0.05))
+        full["g_attn"].append(bf(rng, D, scale=0.1, base=1.0))
+        full["o"].append(bf(rng, D, H * hd, scale=0.05))
+        full["g_mlp"].append(bf(rng, D, scale=0.1, base=1.0))
+        full["gate"].append(bf(rng, I, D, scale=0.05))
+        full["up"].append(bf(rng, I, D, scale=0.05))
+        full["down"].append(bf(rng, D, I, scale=0.05))
+    full["g_final"] = bf(rng, D, scale=0.1, base=1.0)
+    full["lm_head"] = bf(rng, V, D, scale=0.05)
+    full["embed"] = bf(rng, V, D)
+    return shape, full
+
+
+def test_decode_steps_match_oracle(torch_cuda):
+    """Three graph-replayed decode steps of a 2-layer model, 5 sequences at
+    ragged positions, against the oracle step by step (the oracle's token is
+    fed back on both sides, so a near-tie cannot make the runs diverge)."""
+    torch = torch_cuda
+    from python.kinetic_rt.decoder import PagedDecoder, RankWeights
+    rng = np.random.Generator(np.random.PCG64(4))
+    shape, full = tiny_model(rng)
+    B, max_len = 5, 80
+    w = RankWeights.from_full(torch, shape, full, 0, 1)
+    dec = PagedDecoder(torch, shape, w, B, max_len)
+    start_pos = np.array([0, 5, 16, 33, 70])
+    start_tok = rng.integers(0, shape.vocab, size=B)
+    # prefix K/V: random bf16 values in both the oracle's pools and the device's
+    pools = [bf(rng, dec.num_blocks, 16, 2, shape.n_kv_heads, 128) for _ in range(shape.n_layers)]
+    for p, pd in zip(pools, dec.pools):
+        pd.copy_(dev(torch, p.reshape(dec.num_blocks, 16, -1)))
+    dec.start(start_tok, start_pos)
+    table = dec.block_table.cpu().numpy()
+    cos, sin = fused_layer.rope_tables(np.arange(max_len), 128, shape.rope_theta)
+    graph = dec.capture()
+    h = full["embed"][start_tok]
+    pos = start_pos.copy()
+    for step in range(3):
+        logits, tok, h_next = odec.decode_step(full, h, pos, table, pools, cos, sin, shape.n_heads,
+                                               shape.n_kv_heads, 16)
+        dec.next_input.copy_(torch.from_numpy(tok.astype(np.int32)))
+        graph.replay()
+        dec.check_status()
+        got_tok = dec.tokens.cpu().numpy()
+        top2 = np.sort(logits, -1)[:, -2:]
+        near_tie = top2[:, 1] - top2[:, 0] < ATOL + RTOL * np.abs(top2[:, 1])
+        assert np.all((got_tok == tok) | near_tie), (step, got_tok, tok)
+        for li in range(shape.n_layers):  # the step's K/V landed at each sequence's slot
+            got_pool = dec.pools[li].float().cpu().numpy().reshape(pools[li].shape)
+            for s in range(B):
+                blk, off = table[s][pos[s] // 16], pos[s] % 16
+                np.testing.assert_allclose(got_pool[blk, off], pools[li][blk, off], atol=ATOL, rtol=RTOL)
+        np.testing.assert_array_equal(dec.h.float().cpu().numpy(), h_next)
+        assert dec.positions.cpu().numpy().tolist() == (pos + 1).tolist()
+        h, pos = h_next, pos + 1
