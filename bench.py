@@ -1,26 +1,26 @@
 """Benchmark of the decoder hot path on B200.
 
-One step = one Llama-3-8B decoder layer's hot path for a decode batch of 64
-sequences at context 2048, tensor-parallel over N GPUs (one process each):
+Default workload (``--workload stack``): the metric's own configuration,
+decode tokens/s of a Llama-3-8B-shaped stack (random init, bf16): 32 layers,
+hidden 4096, 32/8 heads x 128, SwiGLU 14336, vocabulary 128256, decode batch
+128 at 4096-token contexts, paged KV blocks of 16, greedy sampling, one CUDA
+graph per decode step, tensor-parallel over the N GPUs of the job (one
+process each, torch.distributed.run for N > 1).  One step = one new token for
+each of the 128 sequences through all 32 layers and the lm_head.  The prompt's
+K/V are synthetic (random bf16 written into the paged pools, standing in for
+the prefill of the 4096 random prompt tokens); the timed steps sit in the
+middle of the 256 greedy steps (contexts 4096 .. 4352).  ``value`` = 128 x K /
+device time of K steps (max over ranks); ``config.per_box`` scales it to the
+8 GPUs of a box (8 / N replicas).
 
-  1. fused RMSNorm + QKV projection + RoPE + paged K/V scatter
-     (krt_qkv_rope_decode; Q/K/V heads split over ranks, no collective)
-  2. o_proj   row-parallel GEMM fused with the allreduce (K = 4096 / N)
-  3. down_proj row-parallel GEMM fused with the allreduce (K = 14336 / N)
+``--workload layer``: one decoder layer's hot path at decode batch 64 (fused
+QKV+RoPE+KV scatter, o_proj and down_proj GEMM+allreduce), the kernels the
+scope table names, with their own per-kernel rooflines.
+``--workload prefill``: the fused QKV prefill kernel alone (TFLOP/s).
 
-Inputs are synthetic (seeded N(0,1) activations, N(0, 0.02) weights,
-gamma = 1 + N(0, 0.1), block tables a seeded permutation of the pool).  Each
-step uses the weights of a different layer, cycling over enough layers that
-the weights touched between two uses of a layer exceed the 126 MB L2.
-Steps are CUDA-graph replays (8 steps per graph, the kernels chained by
-programmatic dependent launch); the timed region is bracketed by a barrier
-and device synchronisation and timed with CUDA events, max over ranks.
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl krt|reference] [--workload stack|layer|prefill]
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl krt|reference]
-  python bench.py --workload prefill     # the fused QKV prefill kernel alone (TFLOP/s)
-
-For N > 1 launch one process per GPU with torch.distributed.run.  Prints one
-JSON line on rank 0.
+Prints one JSON line on rank 0.
 """
 import argparse
 import json
@@ -35,8 +35,9 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "kinetic-rt_b200"))
 
 METRIC = "decode tokens/s per box at TP=1/2/4/8; fused QKV+RoPE & GEMM+AR % roofline"
-HIDDEN, N_HEADS, N_KV, HEAD_DIM, INTER = 4096, 32, 8, 128, 14336
-BATCH, CTX, BLOCK = 64, 2048, 16
+HIDDEN, N_HEADS, N_KV, HEAD_DIM, INTER, VOCAB, LAYERS = 4096, 32, 8, 128, 14336, 128256, 32
+BATCH, CTX, BLOCK = 64, 2048, 16              # --workload layer
+STACK_BATCH, PROMPT, GEN_STEPS = 128, 4096, 256  # --workload stack
 L2_BYTES = 126 * 1024 * 1024
 NVLINK_GBS = 770.0  # measured B200 peer-copy bandwidth per direction over NVLink 5 (900 GB/s nominal)
 
@@ -128,7 +129,7 @@ def cpu_baseline(seconds=10.0):
         torch_ref.layer_hot_path_ref(x, w_qkv, gamma, cos, sin, attn, w_o, act, w_d, N_HEADS, N_KV, HEAD_DIM)
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": BATCH / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": BATCH / dt, "unit": "tokens/s", "cores": os.cpu_count(), "cpu_model": cpu_model(), "kind": "port",
             "sample": f"{n} steps of the full {BATCH}-token layer hot path in torch fp32 (oracle/torch_ref.py), "
                       f"{dt * 1e3:.1f} ms/step"}
 
@@ -464,7 +465,7 @@ def run_krt(args, rank, world, local_rank):
         if rc != 0:
             raise RuntimeError(f"kernel status {bits:#x}")
 
-    base = cpu_baseline() if rank == 0 else None
+    base = cpu_baseline() if rank == 0 and world == 1 else {"value": None, "note": "timed at N=1 only"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s (one decoder layer's hot path)",
@@ -491,6 +492,384 @@ def run_krt(args, rank, world, local_rank):
         comm.close()
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- the stack
+def stack_config(n):
+    return {
+        "workload": (f"Llama-3-8B-shaped decoder stack (random init), decode batch {STACK_BATCH} at contexts "
+                     f"{PROMPT}..{PROMPT + GEN_STEPS} (prompt K/V synthetic), greedy, TP={n}: per layer fused "
+                     "RMSNorm+QKV+RoPE+paged-KV scatter, paged GQA attention, o_proj GEMM+allreduce+residual, "
+                     "RMSNorm+gate/up+SwiGLU, down_proj GEMM+allreduce+residual; then RMSNorm+lm_head+argmax and the "
+                     "next embedding; one CUDA graph per decode step"),
+        "model": "llama-3-8b-shaped", "layers": LAYERS, "global_batch": STACK_BATCH, "seq_len": PROMPT,
+        "gen_steps": GEN_STEPS, "parallelism": f"tp{n}", "hidden": HIDDEN, "heads": f"{N_HEADS}/{N_KV}x{HEAD_DIM}",
+        "intermediate": INTER, "vocab": VOCAB, "kv_block": BLOCK,
+        "per_box": f"value x {8 // n} (8 / TP replicas on one 8-GPU box)" if 8 % n == 0 else None,
+        "l2": "inputs larger than L2: each step streams every layer's weights and the whole KV cache",
+    }
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def cpu_stack_sample(reps=2, attn_seqs=8, ctx=PROMPT + GEN_STEPS // 2):
+    """Bounded sample of the reference's CPU path (torch fp32 on every host
+    core, oracle/torch_ref.py) for one decode step of the stack: the
+    projections of one decoder layer at batch 128 (attention over a 1-token
+    context), attention over the full `ctx`-token context for `attn_seqs`
+    sequences, and the lm_head + argmax at batch 128.  One step =
+    32 x (projections + 128 / attn_seqs x attention) + lm_head."""
+    import torch
+    from oracle import torch_ref
+    from oracle.fused_layer import rope_tables
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    r = lambda *sz, s=0.02: torch.randn(*sz, generator=g) * s
+    B, D, I = STACK_BATCH, HIDDEN, INTER
+    w = dict(w_qkv=r((N_HEADS + 2 * N_KV) * HEAD_DIM, D), g_attn=1 + r(D, s=0.1), w_o=r(D, D), g_mlp=1 + r(D, s=0.1),
+             w_gate=r(I, D), w_up=r(I, D), w_down=r(D, I))
+    cos, sin = (torch.from_numpy(a) for a in rope_tables([ctx] * B, HEAD_DIM, 5e5))
+    h = torch.randn(B, D, generator=g)
+    empty = torch.zeros(B, 0, N_KV, HEAD_DIM)
+    kc = torch.randn(attn_seqs, ctx, N_KV, HEAD_DIM, generator=g)
+    vc = torch.randn(attn_seqs, ctx, N_KV, HEAD_DIM, generator=g)
+    w_lm, g_f = r(VOCAB, D), 1 + r(D, s=0.1)
+
+    def proj():
+        torch_ref.decode_layer_ref(h, w["w_qkv"], w["g_attn"], cos, sin, empty, empty, w["w_o"], w["g_mlp"],
+                                   w["w_gate"], w["w_up"], w["w_down"], N_HEADS, N_KV, HEAD_DIM)
+
+    def attn():
+        hs = h[:attn_seqs]
+        torch_ref.decode_layer_ref(hs, w["w_qkv"], w["g_attn"], cos[:attn_seqs], sin[:attn_seqs], kc, vc, w["w_o"],
+                                   w["g_mlp"], w["w_gate"], w["w_up"], w["w_down"], N_HEADS, N_KV, HEAD_DIM)
+
+    def lm():
+        torch_ref.lm_head_greedy_ref(h, g_f, w_lm)
+
+    def timed(f):
+        f()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            f()
+        return (time.perf_counter() - t0) / reps
+
+    t_proj, t_attn_sub, t_lm = timed(proj), timed(attn), timed(lm)
+    # the attention sample also ran the projections for attn_seqs rows: keep only its attention share
+    t_attn = max(t_attn_sub - t_proj * attn_seqs / B, 0.0) * (B / attn_seqs)
+    step = LAYERS * (t_proj + t_attn) + t_lm
+    return {"value": round(B / step, 3), "unit": "tokens/s", "cores": os.cpu_count(), "cpu_model": cpu_model(),
+            "kind": "port", "step_s": round(step, 3),
+            "sample": (f"torch fp32 (oracle/torch_ref.py), {reps} reps each: one layer's projections at batch {B} "
+                       f"({t_proj * 1e3:.1f} ms), attention over {ctx} tokens for {attn_seqs} sequences scaled x"
+                       f"{B // attn_seqs} ({t_attn * 1e3:.1f} ms), lm_head+argmax ({t_lm * 1e3:.1f} ms); "
+                       f"step = {LAYERS} layers + lm_head")}
+
+
+def tp_parity_check(torch, comm, rank, world):
+    """o_proj / down_proj GEMM + allreduce (+ residual) on seeded inputs against
+    the unsharded fp32 product (torch on this GPU), and bit-identity of the
+    result across ranks.  Every rank generates the same full X, W and
+    residual on the host and keeps its torch.chunk(dim=1) shard
+    (scripts/export_hf.py:62-65)."""
+    from python.kinetic_rt import _lib
+    ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    worst, ok, same = 0.0, True, True
+    for (T, K, with_res) in ((STACK_BATCH, HIDDEN, True), (STACK_BATCH, INTER, True), (BATCH, INTER, False),
+                             (1, HIDDEN, False)):
+        g = torch.Generator().manual_seed(K + T)
+        x = torch.randn(T, K, generator=g).to(torch.bfloat16).cuda()
+        w = (torch.randn(HIDDEN, K, generator=g) * 0.02).to(torch.bfloat16).cuda()
+        res = torch.randn(T, HIDDEN, generator=g).to(torch.bfloat16).cuda()
+        step = -(-K // world)
+        lo, hi = rank * step, min((rank + 1) * step, K)
+        xs, wsh = x[:, lo:hi].contiguous(), w[:, lo:hi].contiguous()
+        y = res.clone() if with_res else torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
+        args = _lib.gemm_ar_args(xs, wsh, y, ws, residual=y if with_res else None)
+        _lib.rowparallel_gemm_ar(comm.handle if comm is not None else None, args)
+        rc, bits = _lib.read_status(ws)
+        ref = x.float() @ w.float().t() + (res.float() if with_res else 0)
+        err = (y.float() - ref).abs()
+        worst = max(worst, float(err.max()))
+        ok = ok and bool((err <= 2e-2 + 1e-2 * ref.abs()).all()) and rc == 0
+        if world > 1:
+            import torch.distributed as dist
+            allv = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(allv, y)
+            same = same and all(torch.equal(a.view(torch.int16), allv[0].view(torch.int16)) for a in allv)
+    return {"checked": True, "cases": "o_proj/down_proj at 128 tokens with residual, down_proj at 64, o_proj at 1",
+            "max_abs": round(worst, 5), "within_tolerance": ok, "ranks_identical": same,
+            "tolerance": "max-abs 2e-2 + rel 1e-2 vs unsharded fp32"}
+
+
+def stack_kernel_bytes(world, ctx):
+    """Algorithmic bytes per launch of each kernel of the decode step (this
+    rank's share): every input read once, every output written once."""
+    B, D = STACK_BATCH, HIDDEN
+    hq, hkv, ir = N_HEADS // world, N_KV // world, INTER // world
+    vr = -(-VOCAB // world)
+    qkv_rows = (hq + 2 * hkv) * HEAD_DIM
+    return {
+        "qkv_rope_decode": (qkv_rows * D * 2 + B * D * 2 + B * hq * HEAD_DIM * 2 + B * 2 * hkv * HEAD_DIM * 2,
+                            "W_qkv shard + x read, q + new K/V written"),
+        "paged_attention": (B * ctx * hkv * HEAD_DIM * 2 * 2 + 2 * B * hq * HEAD_DIM * 2,
+                            "K/V of every context token read, q read, output written"),
+        "o_proj_gemm_ar": (D * hq * HEAD_DIM * 2 + B * hq * HEAD_DIM * 2 + 2 * B * D * 2,
+                           "W_o shard + x + residual read, h written"),
+        "gate_up_swiglu": (2 * ir * D * 2 + B * D * 2 + B * ir * 2, "W_gate|up shard + x read, act written"),
+        "down_proj_gemm_ar": (D * ir * 2 + B * ir * 2 + 2 * B * D * 2, "W_down shard + act + residual read, h written"),
+        "lm_head_argmax": (vr * D * 2 + B * D * 2, "lm_head shard + x read"),
+        "greedy_step": (B * D * 2 * 2, "embedding rows read, h written"),
+    }
+
+
+def run_stack(args, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    comm = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=120))
+        from python.kinetic_rt.dist import TPComm
+        comm = TPComm(rank, world, max_n_out=HIDDEN)
+    from python.kinetic_rt.decoder import LLAMA3_8B, PagedDecoder, RankWeights
+    parity = tp_parity_check(torch, comm, rank, world)
+    K, W = args.steps, args.warmup
+    B = STACK_BATCH
+    # the position the first (eager) step processes: the timed steps sit in
+    # the middle of the GEN_STEPS greedy steps after the prompt
+    first = PROMPT + max(0, (GEN_STEPS - K) // 2 - W - 1)
+    e2e_steps = min(K, 64)
+    max_len = max(PROMPT + GEN_STEPS, first + 1 + W + K + e2e_steps + 8)
+    weights = RankWeights.random(torch, LLAMA3_8B, rank, world, seed=0)
+    dec = PagedDecoder(torch, LLAMA3_8B, weights, B, max_len, comm, rank, world)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    dec.pools[0].copy_(torch.randn(dec.pools[0].shape, generator=g, device="cuda").to(torch.bfloat16))
+    for pool in dec.pools[1:]:
+        pool.copy_(dec.pools[0])
+    start = torch.randint(0, VOCAB, (B,), generator=torch.Generator().manual_seed(11))
+    dec.start(start, [first] * B)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        dec.step()  # first call of every entry point outside the capture
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    dec.check_status()
+    graph = dec.capture()
+    for _ in range(W):
+        graph.replay()
+    dec.check_status()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.05)
+    barrier(torch, world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(K):
+        graph.replay()
+    b.record()
+    barrier(torch, world)
+    clk = clocks.stop()
+    dec.check_status()
+    ms = max_over_ranks(torch, a.elapsed_time(b), world)
+    ms_step = ms / K
+    value = B * K / (ms * 1e-3)
+    if world > 1:
+        import torch.distributed as dist
+        toks = [torch.empty_like(dec.tokens) for _ in range(world)]
+        dist.all_gather(toks, dec.tokens)
+        hs = [torch.empty_like(dec.h) for _ in range(world)]
+        dist.all_gather(hs, dec.h)
+        parity["step_tokens_identical"] = all(torch.equal(t, toks[0]) for t in toks)
+        parity["step_hidden_identical"] = all(torch.equal(x.view(torch.int16), hs[0].view(torch.int16)) for x in hs)
+    ctx_mid = first + 1 + W + K // 2
+
+    # per-kernel device time: one graph per kernel kind over all layers
+    hbm, peak_kind = peaks()
+    traffic = {}
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            traffic = json.load(f)
+    except Exception:
+        pass
+    kbytes = stack_kernel_bytes(world, ctx_mid)
+    names = ["qkv_rope_decode", "paged_attention", "o_proj_gemm_ar", "gate_up_swiglu", "down_proj_gemm_ar"]
+    kernels = []
+
+    def time_graph(fn, launches, reps):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        gr.replay()
+        barrier(torch, world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        barrier(torch, world)
+        us = max_over_ranks(torch, e0.elapsed_time(e1), world) * 1e3 / (reps * launches)
+        del gr
+        return us
+
+    saved_pos = dec.positions.clone()
+    for part, name in enumerate(names):
+        us = time_graph(lambda: [dec.layer(li, parts=(part,)) for li in range(LAYERS)], LAYERS, 3)
+        kernels.append((name, us))
+    kernels.append(("lm_head_argmax", time_graph(lambda: _lm(dec), 1, 20)))
+    kernels.append(("greedy_step", time_graph(lambda: _greedy(dec), 1, 20)))
+    dec.positions.copy_(saved_pos)
+    dec.seq_lens.copy_(saved_pos + 1)
+    dec.check_status()
+    klist = []
+    for name, us in kernels:
+        nbytes, what = kbytes[name]
+        ach = nbytes / (us * 1e-6) / 1e9
+        entry = {"kernel": name, "bound": "hbm", "us": round(us, 3), "algorithmic_bytes": int(nbytes), "bytes": what,
+                 "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+                 "traffic": traffic.get(f"stack_{name}_tp{world}"), "launches_per_step": LAYERS if name in names else 1}
+        if name.endswith("gemm_ar") and world > 1:
+            wire = 2 * (world - 1) / world * B * HIDDEN * 4
+            target = max(nbytes / hbm / 1e3, wire / NVLINK_GBS / 1e3)
+            entry.update({"nvlink_wire_bytes_per_gpu": int(wire), "roofline_us": round(target, 3),
+                          "frac_of_roofline": round(target / us, 4)})
+        klist.append(entry)
+    step_bytes = sum(e["algorithmic_bytes"] * e["launches_per_step"] for e in klist)
+    dominant = max(klist, key=lambda e: e["us"] * e["launches_per_step"])
+
+    # end to end through the driver's public API: every step the host copies
+    # the step's input tokens (pinned) to the device, replays the step and
+    # reads the chosen tokens back, waiting for them (a serving loop)
+    feed = torch.empty(e2e_steps + 1, B, dtype=torch.int32, pin_memory=True)
+    got = torch.empty(e2e_steps, B, dtype=torch.int32, pin_memory=True)
+    feed[0].copy_(dec.tokens.cpu())
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        dec.next_input.copy_(feed[i], non_blocking=True)
+        graph.replay()
+        got[i].copy_(dec.tokens, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        feed[i + 1].copy_(got[i])
+    e1.record()
+    barrier(torch, world)
+    e2e_ms = max_over_ranks(torch, e0.elapsed_time(e1), world) / e2e_steps
+    dec.check_status()
+    prefill = prefill_entry(torch, rank, world)
+    del graph
+    base = None
+    if world == 1:
+        base = cpu_stack_sample()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "decode tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, random prompt ids and prompt K/V)", "config": stack_config(world),
+            "per_box_tokens_per_s": round(value * 8 / world, 1) if 8 % world == 0 else None,
+            "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "decode tokens/s",
+                    "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4,
+                    "how": "per step: pinned-host tokens -> device, graph replay, chosen tokens -> pinned host, "
+                           "host waits and feeds them to the next step"},
+            "gpu_launches": dec.launches_per_step * K,
+            "roofline": {"bound": "hbm", "kernel": dominant["kernel"], "achieved": dominant["achieved"], "peak": hbm,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["frac"],
+                         "traffic": dominant["traffic"]},
+            "step": {"algorithmic_bytes_per_gpu": int(step_bytes),
+                     "achieved_GBps": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
+                     "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4), "context_mid": ctx_mid},
+            "kernels": klist + ([prefill] if prefill else []),
+            "parity": parity,
+            "cpu_baseline": base if base else {"value": None, "note": "timed at N=1 only (rank 0 alone on the host)"},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    bad = not (parity["within_tolerance"] and parity["ranks_identical"] and parity.get("step_tokens_identical", True)
+               and parity.get("step_hidden_identical", True))
+    if comm is not None:
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    if bad:
+        print("parity check failed", file=sys.stderr)
+        sys.exit(3)
+
+
+def _lm(dec):
+    from python.kinetic_rt import _lib
+    _lib.lm_head_argmax(dec.lm_args)
+
+
+def _greedy(dec):
+    from python.kinetic_rt import _lib
+    _lib.greedy_step(dec.comm_handle, dec.greedy_args)
+
+
+def prefill_entry(torch, rank, world, seqs=8, seq_len=2048):
+    """The prefill kernel (fused QKV + RoPE + paged scatter) on this rank's
+    head shard for 8 x 2048 tokens, as a kernels entry in TFLOP/s."""
+    from python.kinetic_rt import _lib
+    from python.kinetic_rt.decoder import rope_cache
+    T = seqs * seq_len
+    hq, hkv = N_HEADS // world, N_KV // world
+    rows = (hq + 2 * hkv) * HEAD_DIM
+    g = torch.Generator(device="cuda").manual_seed(99 + rank)
+    x = torch.randn(T, HIDDEN, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(rows, HIDDEN, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    gamma = torch.ones(HIDDEN, dtype=torch.bfloat16, device="cuda")
+    cos, sin = rope_cache(torch, seq_len, HEAD_DIM, 5e5)
+    positions = torch.arange(seq_len, dtype=torch.int32, device="cuda").repeat(seqs)
+    token_seq = torch.arange(seqs, dtype=torch.int32, device="cuda").repeat_interleave(seq_len)
+    nblk = T // BLOCK
+    table = torch.randperm(nblk, generator=torch.Generator().manual_seed(5)).to(torch.int32).view(seqs, -1).cuda()
+    pool = torch.zeros(nblk, BLOCK, 2 * hkv * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(T, hq * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+    ws = torch.zeros(_lib.prefill_workspace_bytes(T, HIDDEN, hq, hkv), dtype=torch.uint8, device="cuda")
+    a = _lib.paged_args(x, w, None, gamma, cos, sin, positions, token_seq, table, pool, q, hq, hkv, nblk, BLOCK, ws)
+    _lib.qkv_rope_prefill(a)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(4):
+            _lib.qkv_rope_prefill(a)
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    rc, bits = _lib.read_status(ws)
+    if rc != 0:
+        raise RuntimeError(f"prefill status {bits:#x}")
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        peak = 1590.0
+    tflops = 2.0 * T * HIDDEN * rows / (ms * 1e-3) / 1e12
+    return {"kernel": "qkv_rope_prefill", "bound": "tensor", "us": round(ms * 1e3, 1),
+            "algorithmic_flops": int(2 * T * HIDDEN * rows), "achieved": round(tflops, 1), "peak": peak,
+            "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "launches_per_step": 0,
+            "shape": f"{seqs} x {seq_len} tokens, this rank's {hq}/{hkv} heads (not part of the decode step)"}
 
 
 def run_prefill(args, rank, world, local_rank):
@@ -584,6 +963,8 @@ def run_reference(args, rank, world):
     """The reference's own CPU path (torch fp32, every host core), rank 0 only."""
     if rank != 0:
         return
+    if args.workload == "stack":
+        return run_reference_stack(args, world)
     import torch
     from oracle import torch_ref
     from oracle.fused_layer import rope_tables
@@ -621,15 +1002,40 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
+def run_reference_stack(args, world):
+    """The stack's metric on the CPU path: each of min(K, 3) samples is one
+    bounded sample (cpu_stack_sample) of a decode step; value = tokens/s."""
+    n = max(1, min(args.steps, 3))
+    samples = [cpu_stack_sample(reps=1) for _ in range(n)]
+    step = sorted(x["step_s"] for x in samples)[len(samples) // 2]
+    value = STACK_BATCH / step
+    base = dict(samples[0])
+    base.update(value=round(value, 3), sample=f"median of {n} samples; each: " + base["sample"])
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "decode tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step * 1e3, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights, random prompt K/V)", "config": stack_config(world),
+        "cpu_baseline": base,
+        "e2e": {"value": round(value, 3), "unit": "decode tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 64 decode steps of the stack, 20000 layer steps)")
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["krt", "reference"], default="krt")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode: the decoder-layer step (default); prefill: the fused QKV prefill kernel alone")
+    ap.add_argument("--workload", choices=["stack", "layer", "prefill"], default="stack",
+                    help="stack: decode steps of the Llama-3-8B-shaped stack (default); layer: one decoder layer's "
+                         "hot path; prefill: the fused QKV prefill kernel alone")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 64 if args.workload == "stack" else 20000
+    if args.warmup is None:
+        args.warmup = 8 if args.workload == "stack" else 50
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
@@ -641,8 +1047,10 @@ def main():
         run_reference(args, rank, world)
     elif args.workload == "prefill":
         run_prefill(args, rank, world, local_rank)
-    else:
+    elif args.workload == "layer":
         run_krt(args, rank, world, local_rank)
+    else:
+        run_stack(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":

@@ -166,9 +166,20 @@ KRT_API int krt_qkv_rope_prefill(const krt_qkv_paged_args* args, void* stream);
  *    before any stream capture on the device.
  *  - Every call on a device shares the one array and clears its header at the
  *    start; calls that can overlap on the GPU (different streams without
- *    ordering) race on it.  The status word is not readable by the caller.
+ *    ordering) race on it.  The status word of the last call is read with
+ *    krt_qkv_rope_decode_noalloc_status.
+ *  - Arguments are checked before anything reaches the GPU: a rejected call
+ *    leaves the array untouched.
+ *  - After cudaDeviceReset the array's address is looked up again (the
+ *    context id changed); that first call after a reset, too, must come
+ *    before any stream capture.
  *  - Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
 KRT_API int krt_qkv_rope_decode_noalloc(const krt_qkv_paged_args* args, void* stream);
+
+/* The status word of the library's fixed decode scratch on the current
+ * device, as krt_read_status reports a workspace's (synchronises the stream,
+ * clears the word).  Allocates nothing. */
+KRT_API int krt_qkv_rope_decode_noalloc_status(void* stream, int32_t* bits);
 
 /* Copy the device status word of a workspace to the host (synchronises the
  * stream), clear it, and return KRT_OK or KRT_ERR_DEVICE with the bits in

@@ -234,7 +234,7 @@ extern "C" int krt_fused_rmsnorm_qkv_rope(const krt_qkv_rope_args* a, void* stre
 // ------------------------------------------------------------------- paged
 namespace {
 
-int paged_common_checks(const krt_qkv_paged_args* a, const char* name) {
+int paged_common_checks(const krt_qkv_paged_args* a, const char* name, bool need_workspace = true) {
   if (!a) return set_error(KRT_ERR_INVALID, "%s: args is NULL", name);
   if (!a->x || !a->qkv_weight || !a->rms_weight || !a->rope_cos || !a->rope_sin || !a->positions ||
       !a->token_seq || !a->block_table || !a->kv_pool || !a->q_out)
@@ -259,7 +259,7 @@ int paged_common_checks(const krt_qkv_paged_args* a, const char* name) {
   if (a->max_position <= 0 || a->num_seqs <= 0 || a->block_table_stride <= 0 || a->num_blocks <= 0 ||
       a->tokens_per_block <= 0)
     return set_error(KRT_ERR_INVALID, "%s: paged-cache geometry must be positive", name);
-  if (!a->workspace) return set_error(KRT_ERR_WORKSPACE, "%s: workspace is NULL", name);
+  if (need_workspace && !a->workspace) return set_error(KRT_ERR_WORKSPACE, "%s: workspace is NULL", name);
   return KRT_OK;
 }
 
@@ -337,6 +337,18 @@ DecodeCfg decode_config(int heads, int num_kb, int n_pad, bool whole_tiles = fal
 }
 
 }  // namespace
+
+namespace krt {
+// Argument checks of the decode path without the workspace (for callers
+// that supply the workspace themselves); KRT_OK or an error with `name`.
+int decode_args_check(const krt_qkv_paged_args* a, const char* name) {
+  int rc = paged_common_checks(a, name, false);
+  if (rc) return rc;
+  if (a->num_tokens > 256)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: num_tokens must be <= 256 (use the prefill path)", name);
+  return KRT_OK;
+}
+}  // namespace krt
 
 extern "C" size_t krt_qkv_rope_decode_workspace_size(int32_t num_tokens, int32_t d_model, int32_t n_heads,
                                                      int32_t n_kv_heads, int32_t head_dim) {

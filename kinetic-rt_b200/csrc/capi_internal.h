@@ -8,6 +8,8 @@
 #include <cstdint>
 #include <initializer_list>
 
+struct krt_qkv_paged_args;
+
 namespace krt {
 
 struct GenericArgs;
@@ -23,6 +25,9 @@ int make_tmap_bf16_5d_strided(CUtensorMap* map, const void* base, std::initializ
                               std::initializer_list<uint64_t> strides, std::initializer_list<uint32_t> box);
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                       uint32_t box_rows);
+
+// capi.cu: argument checks of krt_qkv_rope_decode, workspace excluded
+int decode_args_check(const krt_qkv_paged_args* a, const char* name);
 
 // qkv_generic.cu
 cudaError_t launch_qkv_rope_generic(const GenericArgs& a, int dtype, int freqs_dtype, int grid, int block,

@@ -15,8 +15,10 @@
 // code only sees a host-side stand-in for its name, so the device address is
 // looked up once per device (cudaGetSymbolAddress, with that device current)
 // the first time the entry point runs there, and cached.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -32,23 +34,54 @@ constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
+// Identity of the current CUDA context (cuCtxGetId), or 0 when the driver
+// cannot tell.  A device reset destroys the primary context and the module
+// with it; the next context gets a new id, so a cached array address is
+// looked up again instead of pointing into freed memory.
+unsigned long long current_context_id() {
+  typedef CUresult (*GetCurrentFn)(CUcontext*);
+  typedef CUresult (*GetIdFn)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kNoAllocMaxDevices] = {};
+unsigned long long g_scratch_ctx[kNoAllocMaxDevices] = {};
 
-// Device address of g_decode_scratch on the current device.
-int scratch_for_current_device(void** out) {
+// Device address of g_decode_scratch on the current device: looked up with
+// cudaGetSymbolAddress the first time per device (and again after the
+// device's context was replaced), then cached.
+int scratch_for_current_device(const char* name, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_decode_noalloc: cudaGetDevice");
+  if (e != cudaSuccess) return cuda_error(e, name);
   if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return set_error(KRT_ERR_UNSUPPORTED, "krt_qkv_rope_decode_noalloc: device %d beyond %d", dev,
-                     kNoAllocMaxDevices);
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: device %d beyond %d", name, dev, kNoAllocMaxDevices);
+  const unsigned long long ctx = current_context_id();  // 0 until the runtime bound a context here
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  if (g_scratch_addr[dev] == nullptr || ctx == 0 || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_decode_noalloc: cudaGetSymbolAddress");
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);  // binds the device's primary context
+    if (e != cudaSuccess) return cuda_error(e, name);
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = current_context_id();
   }
   *out = g_scratch_addr[dev];
   return KRT_OK;
@@ -60,24 +93,44 @@ int scratch_for_current_device(void** out) {
 using namespace krt;
 
 extern "C" int krt_qkv_rope_decode_noalloc(const krt_qkv_paged_args* args, void* stream) {
-  if (!args) return set_error(KRT_ERR_INVALID, "krt_qkv_rope_decode_noalloc: args is NULL");
+  const char* name = "krt_qkv_rope_decode_noalloc";
+  // Every argument check comes first: a rejected call touches neither the
+  // GPU nor the shared array.
+  int rc = decode_args_check(args, name);
+  if (rc) return rc;
   const size_t need = krt_qkv_rope_decode_workspace_size(args->num_tokens, args->d_model, args->n_heads,
                                                          args->n_kv_heads, args->head_dim);
-  if (need > kNoAllocScratchBytes)
+  if (need == 0 || need > kNoAllocScratchBytes)
     return set_error(KRT_ERR_UNSUPPORTED,
-                     "krt_qkv_rope_decode_noalloc: this call needs %zu bytes of scratch (num_tokens %d, d_model %d); "
+                     "%s: this call needs %zu bytes of scratch (num_tokens %d, d_model %d); "
                      "the library's fixed scratch holds %zu bytes",
-                     need, args->num_tokens, args->d_model, kNoAllocScratchBytes);
+                     name, need, args->num_tokens, args->d_model, kNoAllocScratchBytes);
   void* scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
+  rc = scratch_for_current_device(name, &scratch);
   if (rc) return rc;
   // The status word and the header must start at zero; the rest of the
   // scratch is fully rewritten by every call.
   cudaError_t e = cudaMemsetAsync(scratch, 0, kWsHeaderBytes, (cudaStream_t)stream);
-  if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_decode_noalloc: clearing the scratch header");
+  if (e != cudaSuccess) return cuda_error(e, name);
   krt_qkv_paged_args a;
   std::memcpy(&a, args, sizeof(a));
   a.workspace = scratch;
   a.workspace_bytes = kNoAllocScratchBytes;
-  return krt_qkv_rope_decode(&a, stream);
+  rc = krt_qkv_rope_decode(&a, stream);
+  if (rc) {
+    // keep the failing call's message but name this entry point
+    char msg[1024];
+    std::snprintf(msg, sizeof(msg), "%s", krt_last_error());
+    return set_error(rc, "%s: %s", name, msg);
+  }
+  return KRT_OK;
+}
+
+extern "C" int krt_qkv_rope_decode_noalloc_status(void* stream, int32_t* bits) {
+  const char* name = "krt_qkv_rope_decode_noalloc_status";
+  if (!bits) return set_error(KRT_ERR_INVALID, "%s: bits is NULL", name);
+  void* scratch = nullptr;
+  int rc = scratch_for_current_device(name, &scratch);
+  if (rc) return rc;
+  return krt_read_status(scratch, stream, bits);
 }

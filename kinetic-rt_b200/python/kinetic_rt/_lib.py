@@ -110,6 +110,7 @@ SIGNATURES = {
     "krt_qkv_rope_decode_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     "krt_qkv_rope_decode": (ctypes.c_int, [ctypes.POINTER(QkvPagedArgs), _vp]),
     "krt_qkv_rope_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(QkvPagedArgs), _vp]),
+    "krt_qkv_rope_decode_noalloc_status": (ctypes.c_int, [_vp, ctypes.POINTER(_i32)]),
     "krt_qkv_rope_prefill_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     "krt_qkv_rope_prefill": (ctypes.c_int, [ctypes.POINTER(QkvPagedArgs), _vp]),
     "krt_read_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i32)]),

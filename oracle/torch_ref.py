@@ -39,3 +39,28 @@ def layer_hot_path_ref(x, w_qkv, gamma, cos, sin, attn_out, w_o, mlp_act, w_down
     y_o = F.linear(attn_out, w_o)
     y_d = F.linear(mlp_act, w_down)
     return q, k, v, y_o, y_d
+
+
+def decode_layer_ref(h, w_qkv, g_attn, cos, sin, k_cache, v_cache, w_o, g_mlp, w_gate, w_up, w_down,
+                     n_heads, n_kv_heads, head_dim, eps=1e-5):
+    """One Llama decoder layer for one new token per sequence, on the CPU in
+    fp32: RMSNorm + QKV + RoPE (tests/test_fusion.py:11-51 per head), attention
+    over the cached K/V plus the new token's, o_proj + residual, RMSNorm,
+    SwiGLU MLP + residual.  h [B, D]; k_cache / v_cache [B, ctx, Hkv, hd]."""
+    q, k, v = qkv_rope_ref(h, w_qkv, g_attn, cos, sin, n_heads, n_kv_heads, head_dim, eps)
+    B = h.shape[0]
+    kk = torch.cat([k_cache, k[:, None]], 1)  # [B, ctx + 1, Hkv, hd]
+    vv = torch.cat([v_cache, v.view(B, 1, n_kv_heads, head_dim)], 1)
+    rep = n_heads // n_kv_heads
+    kk = kk.permute(0, 2, 1, 3).repeat_interleave(rep, 1)  # [B, H, ctx + 1, hd]
+    vv = vv.permute(0, 2, 1, 3).repeat_interleave(rep, 1)
+    a = F.scaled_dot_product_attention(q[:, :, None, :], kk, vv)[:, :, 0, :].reshape(B, -1)
+    h = h + F.linear(a, w_o)
+    x = rms_norm_ref(h, g_mlp, eps)
+    return h + F.linear(F.silu(F.linear(x, w_gate)) * F.linear(x, w_up), w_down)
+
+
+def lm_head_greedy_ref(h, g_final, w_lm, eps=1e-5):
+    """Final RMSNorm, lm_head and the greedy choice (python/kinetic_rt/
+    orchestrator.py:442-444: argmax of the last token's logits)."""
+    return torch.argmax(F.linear(rms_norm_ref(h, g_final, eps), w_lm), dim=-1)

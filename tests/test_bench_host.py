@@ -38,7 +38,7 @@ def test_gpu_local_cpus_unknown_device(tmp_path):
 def test_reference_arm_prints_the_contract_line():
     """`bench.py --impl reference` (the CPU path, no GPU) prints one JSON line
     with the keys the driver reads, on the same metric and config as the
-    GPU arm."""
+    GPU arm's default (stack) workload."""
     import json
     import subprocess
     import sys
@@ -53,5 +53,24 @@ def test_reference_arm_prints_the_contract_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["value"] > 0
-    assert d["config"] == bench.workload_config(1)
+    assert d["config"] == bench.stack_config(1)
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["cpu_baseline"]["kind"] == "port"
+    assert d["cpu_baseline"]["cores"] == os.cpu_count()
+
+
+def test_stack_kernel_bytes_cover_the_step():
+    """Per-GPU algorithmic bytes of one decode step at TP=1 and context 4224:
+    the weights (about 15 GB without the embedding) plus the KV cache read
+    (about 71 GB)."""
+    kb = bench.stack_kernel_bytes(1, 4224)
+    per_step = sum(v[0] * (bench.LAYERS if k not in ("lm_head_argmax", "greedy_step") else 1) for k, v in kb.items())
+    assert 85e9 < per_step < 88e9
+    kb8 = bench.stack_kernel_bytes(8, 4224)
+    kv = lambda kb, heads: kb["paged_attention"][0] - 2 * 128 * heads * 128 * 2  # the K/V part
+    assert kv(kb, 32) == 8 * kv(kb8, 4)
+
+
+def test_stack_config_names_the_metric_workload():
+    c = bench.stack_config(8)
+    assert c["layers"] == 32 and c["global_batch"] == 128 and c["parallelism"] == "tp8"
+    assert "per_box" in c and c["vocab"] == 128256

@@ -41,4 +41,5 @@ def test_version_and_error_strings():
         pytest.skip("libkrt.so not built")
     h = _lib.lib()
     assert b"sm_100a" in h.krt_version()
+    assert h.krt_comm_destroy(None) == 0   # a successful call clears this thread's message
     assert h.krt_last_error() == b""

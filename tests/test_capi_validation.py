@@ -65,6 +65,33 @@ def test_decode_rejects_bad_arguments(over, code, text):
     assert text in msg and msg.startswith("krt_qkv_rope_decode")
 
 
+@pytest.mark.parametrize("over,code,text", [
+    (dict(x=None), _lib.KRT_ERR_INVALID, "required pointer"),
+    (dict(num_tokens=0), _lib.KRT_ERR_INVALID, "must be positive"),
+    (dict(head_dim=64), _lib.KRT_ERR_UNSUPPORTED, "head_dim"),
+    (dict(d_model=4000), _lib.KRT_ERR_UNSUPPORTED, "multiple of 64"),
+    (dict(x_stride=4092), _lib.KRT_ERR_INVALID, "x_stride"),
+    (dict(q_stride=100), _lib.KRT_ERR_INVALID, "q_stride"),
+    (dict(x=FAKE + 4), _lib.KRT_ERR_INVALID, "16-byte aligned"),
+    (dict(num_blocks=0), _lib.KRT_ERR_INVALID, "geometry"),
+    (dict(num_tokens=257), _lib.KRT_ERR_UNSUPPORTED, "prefill path"),
+    (dict(num_tokens=256, d_model=8192, x_stride=8192), _lib.KRT_ERR_UNSUPPORTED, "scratch"),
+])
+def test_decode_noalloc_rejects_bad_arguments_before_any_gpu_call(over, code, text):
+    """The no-allocation entry point checks every argument (its workspace
+    fields are ignored) before it looks up or clears the shared scratch, so
+    these rejections need no GPU and report its own name."""
+    a = _paged(workspace=None, workspace_bytes=0, **over)
+    rc, msg = _call("krt_qkv_rope_decode_noalloc", ctypes.byref(a), None)
+    assert rc == code, msg
+    assert text in msg and msg.startswith("krt_qkv_rope_decode_noalloc")
+
+
+def test_decode_noalloc_status_rejects_null():
+    rc, msg = _call("krt_qkv_rope_decode_noalloc_status", None, None)
+    assert rc == _lib.KRT_ERR_INVALID and msg.startswith("krt_qkv_rope_decode_noalloc_status")
+
+
 def test_prefill_rejects_a_small_workspace():
     a = _paged(num_tokens=4096, workspace_bytes=4096)
     rc, msg = _call("krt_qkv_rope_prefill", ctypes.byref(a), None)

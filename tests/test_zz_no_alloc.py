@@ -82,3 +82,27 @@ def test_noalloc_rejects_oversized_calls(torch_cuda):
     rc = _call_noalloc(krt, a)
     assert rc == krt.KRT_ERR_UNSUPPORTED
     assert b"scratch" in krt.lib().krt_last_error()
+
+
+def test_noalloc_status_reports_a_bad_block(torch_cuda):
+    """The status word lives in the shared scratch; the caller reads it with
+    krt_qkv_rope_decode_noalloc_status.  A token whose block id lies outside
+    the pool sets bit 8, the other tokens still land, and reading clears it."""
+    torch = torch_cuda
+    from python.kinetic_rt import _lib as krt
+    case = PagedCase(4, 1, 512, 4, 2, seed=3, ctx=40)
+    d = case.to_device(torch)
+    bt = d["block_table"].clone()
+    bt[2, :] = case.num_blocks + 5  # outside the pool
+    d["block_table"] = bt
+    assert _call_noalloc(krt, _args(krt, d, case, None)) == 0, krt.lib().krt_last_error().decode()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    bits = ctypes.c_int32(0)
+    rc = krt.lib().krt_qkv_rope_decode_noalloc_status(stream, ctypes.byref(bits))
+    assert rc == krt.KRT_ERR_DEVICE and bits.value & 8
+    pool = d["pool"].view(torch.int16).cpu().numpy().reshape(case.num_blocks * 16, 2, -1)
+    kd = d["k"].view(torch.int16).cpu().numpy()
+    slots = case.slots()
+    for t in (0, 1, 3):
+        np.testing.assert_array_equal(pool[slots[t], 0], kd[t])
+    assert krt.lib().krt_qkv_rope_decode_noalloc_status(stream, ctypes.byref(bits)) == 0 and bits.value == 0
