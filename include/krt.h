@@ -212,6 +212,18 @@ KRT_API int krt_comm_ipc_handle(krt_comm* comm, void* handle_out);
 KRT_API int krt_comm_open_peers(krt_comm* comm, const void* handles);
 KRT_API int krt_comm_destroy(krt_comm* comm);
 
+/* Recovery after a peer wait ran out (status bit 16), e.g. when one rank
+ * skipped or lost a collective call: the exchange epochs of the ranks no
+ * longer agree, and every later fused call would wait out its budget.
+ * A collective: every rank lets its own stream drain and all ranks meet at a
+ * host barrier (so no kernel still writes into a peer's buffer), then each
+ * calls krt_comm_reset, which zeroes this rank's flags, flagged words and
+ * epoch counters (synchronising `stream`), and all meet at a second host
+ * barrier before the next collective (TPComm.reset in python/kinetic_rt/dist.py
+ * does exactly this).  The reference's
+ * mock has no such state (tests/mock_rccl.h:72-74 only times out). */
+KRT_API int krt_comm_reset(krt_comm* comm, void* stream);
+
 /* Allreduce-sum of `count` elements (Communicator::all_reduce_async,
  * src/Communicator.cpp:21-27; every rank's recv receives the elementwise sum
  * of all ranks' send, tests/mock_rccl.h:51-62).  dtype: KRT_DTYPE_FLOAT32

@@ -21,6 +21,7 @@
 #include <mutex>
 #include <tuple>
 #include <new>
+#include <vector>
 
 #include "../../include/krt.h"
 #include "capi_internal.h"
@@ -305,6 +306,17 @@ extern "C" int krt_comm_open_peers(krt_comm* c, const void* handles) {
   return clear_error();
 }
 
+extern "C" int krt_comm_reset(krt_comm* c, void* stream) {
+  if (!c) return set_error(KRT_ERR_INVALID, "krt_comm_reset: communicator is NULL");
+  // Every exchange area of this rank's buffer (flags, flagged words, epoch
+  // counters) back to the state krt_comm_create left it in.
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(c->local, 0, c->L.total, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_comm_reset");
+  return clear_error();
+}
+
 extern "C" int krt_comm_destroy(krt_comm* c) {
   if (!c) return clear_error();
   for (int q = 0; q < c->world; ++q)
@@ -482,32 +494,48 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
   if (a->residual && (reinterpret_cast<uintptr_t>(a->residual) & 15))
     return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: residual must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
+  // Every slice's parameters and tensor maps are built before the first
+  // launch: with a communicator, every rank must make the same launches (the
+  // exchange epochs count them), so a call that fails on the host fails
+  // before any of its kernels run.
+  struct Slice {
+    GemmArParams p;
+    GemmCfg cfg;
+    CUtensorMap tmap_w, tmap_x;
+  };
+  std::vector<Slice> slices;
+  slices.reserve((size_t)(a->num_tokens + 255) / 256);
   for (int t0 = 0; t0 < a->num_tokens; t0 += 256) {
     const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
-    p.num_tokens = T;
-    p.n_pad = (T + 15) / 16 * 16;
-    const GemmCfg cfg = gemm_config(a->n_out, num_kb, p.n_pad, p.comm.world);
-    p.kc = cfg.kc;
-    p.stages = cfg.stages;
-    p.splits = cfg.splits;
+    Slice sl;
+    sl.p = p;
+    sl.p.num_tokens = T;
+    sl.p.n_pad = (T + 15) / 16 * 16;
+    sl.cfg = gemm_config(a->n_out, num_kb, sl.p.n_pad, p.comm.world);
+    sl.p.kc = sl.cfg.kc;
+    sl.p.stages = sl.cfg.stages;
+    sl.p.splits = sl.cfg.splits;
     // L2 prefetch of weight stages ahead of the ring: off by default (it
     // shortens o_proj alone, 10.7 -> 10.3 us, but lengthens the chained
     // decoder-layer step); KRT_L2_PREFETCH_STAGES turns it on.
-    p.prefetch = env_int_value("KRT_L2_PREFETCH_STAGES", 0);
+    sl.p.prefetch = env_int_value("KRT_L2_PREFETCH_STAGES", 0);
     int cols = 32;
-    while (cols < p.n_pad) cols <<= 1;
-    p.tmem_cols = cols;
-    p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
-    p.residual = a->residual ? static_cast<const __nv_bfloat16*>(a->residual) + (size_t)t0 * a->y_stride : nullptr;
+    while (cols < sl.p.n_pad) cols <<= 1;
+    sl.p.tmem_cols = cols;
+    sl.p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
+    sl.p.residual =
+        a->residual ? static_cast<const __nv_bfloat16*>(a->residual) + (size_t)t0 * a->y_stride : nullptr;
     const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
-    CUtensorMap tmap_w, tmap_x;
-    int rc = make_tmap_bf16_3d(&tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local, (uint64_t)a->k_local,
-                               (uint32_t)cfg.tile_m, (uint32_t)p.kc);
+    int rc = make_tmap_bf16_3d(&sl.tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local,
+                               (uint64_t)a->k_local, (uint32_t)sl.cfg.tile_m, (uint32_t)sl.p.kc);
     if (rc) return rc;
-    rc = make_tmap_bf16_3d(&tmap_x, xp, (uint64_t)T, (uint64_t)a->k_local, (uint64_t)a->x_stride, (uint32_t)p.n_pad,
-                           (uint32_t)p.kc);
+    rc = make_tmap_bf16_3d(&sl.tmap_x, xp, (uint64_t)T, (uint64_t)a->k_local, (uint64_t)a->x_stride,
+                           (uint32_t)sl.p.n_pad, (uint32_t)sl.p.kc);
     if (rc) return rc;
-    cudaError_t e = launch_rowparallel_gemm_ar(cfg.tile_m, tmap_w, tmap_x, p, cfg.tiles, s);
+    slices.push_back(sl);
+  }
+  for (const Slice& sl : slices) {
+    cudaError_t e = launch_rowparallel_gemm_ar(sl.cfg.tile_m, sl.tmap_w, sl.tmap_x, sl.p, sl.cfg.tiles, s);
     if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
   }
   return clear_error();

@@ -103,6 +103,36 @@ __device__ __forceinline__ uint64_t* ll_result(const CommView& cv, int holder, i
          ((size_t)tile * kMaxChunks + ch) * (TM / 32 * 128 * 2);
 }
 
+// Polls the stage words of up to four source ranks together (NP word pairs
+// each, pairs 256 words apart): every load of a round is issued before any
+// is checked, so a round costs one memory latency whatever the number of
+// sources.  out[s][2i], out[s][2i + 1] receive source s's words.
+template <int NP>
+__device__ __forceinline__ bool poll_stage_sources(const uint64_t* const* src, int nsrc, uint32_t epoch, uint64_t t0,
+                                                   uint64_t (*out)[2 * NP]) {
+  while (true) {
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      if (s < nsrc) {
+#pragma unroll
+        for (int i = 0; i < NP; ++i)
+          asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];"
+                       : "=l"(out[s][2 * i]), "=l"(out[s][2 * i + 1])
+                       : "l"(src[s] + 256 * i)
+                       : "memory");
+      }
+    bool all = true;
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      if (s < nsrc) {
+#pragma unroll
+        for (int i = 0; i < 2 * NP; ++i) all = all && (uint32_t)(out[s][i] >> 48) == epoch;
+      }
+    if (all) return true;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+  }
+}
+
 // RG bf16 values as RG / 8 16-byte vectors.
 template <int RG>
 __device__ __forceinline__ void store_bf16_rows(__nv_bfloat16* dst, const uint32_t* w) {
@@ -399,18 +429,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int i = 0; i < RG; ++i) acc[i] = 0.f;
           const uint32_t epoch = tl->epoch[ch / nranks];
-          for (int q = 0; q < world; ++q) {
-            uint64_t u[RG / 2];
+          // up to four ranks' words per polling round, added in rank order
+          for (int q0 = 0; q0 < world && ok; q0 += 4) {
+            const int nq = world - q0 < 4 ? world - q0 : 4;
+            const uint64_t* src[4];
 #pragma unroll
-            for (int i = 0; i < RG / 2; ++i) u[i] = 0u;
-            if (ok)
-              ok = poll_words_batch<NP, 48>(ll_stage<TM>(cv, cv.rank, q, tile, ch, epoch) + 2 * ept, 256, epoch, t0, u);
+            for (int s4 = 0; s4 < 4; ++s4)
+              src[s4] = ll_stage<TM>(cv, cv.rank, q0 + (s4 < nq ? s4 : 0), tile, ch, epoch) + 2 * ept;
+            uint64_t u[4][RG / 2];
+            ok = poll_stage_sources<NP>(src, nq, epoch, t0, u);
+            if (!ok) break;
 #pragma unroll
-            for (int i = 0; i < RG / 2; ++i) {
-              const float2 v = f24_pair_unpack(u[i]);
-              acc[2 * i] += v.x;
-              acc[2 * i + 1] += v.y;
-            }
+            for (int s4 = 0; s4 < 4; ++s4)
+              if (s4 < nq) {
+#pragma unroll
+                for (int i = 0; i < RG / 2; ++i) {
+                  const float2 v = f24_pair_unpack(u[s4][i]);
+                  acc[2 * i] += v.x;
+                  acc[2 * i + 1] += v.y;
+                }
+              }
           }
           if (!ok || t >= T) continue;
           add_residual_rows<RG>(acc, p.residual ? p.residual + (size_t)t * p.y_stride + row0 + RG * g : nullptr);

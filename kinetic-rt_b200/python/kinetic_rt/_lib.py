@@ -119,6 +119,7 @@ SIGNATURES = {
     "krt_comm_ipc_handle": (ctypes.c_int, [_vp, _vp]),
     "krt_comm_open_peers": (ctypes.c_int, [_vp, _vp]),
     "krt_comm_destroy": (ctypes.c_int, [_vp]),
+    "krt_comm_reset": (ctypes.c_int, [_vp, _vp]),
     "krt_allreduce": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t, _i32, _vp, _vp]),
     "krt_rowparallel_gemm_ar_workspace_size": (ctypes.c_size_t, []),
     "krt_rowparallel_gemm_ar": (ctypes.c_int, [_vp, ctypes.POINTER(GemmArArgs), _vp]),
@@ -266,6 +267,10 @@ def comm_ipc_handle(comm):
 def comm_open_peers(comm, handles):
     blob = b"".join(handles)
     check(lib().krt_comm_open_peers(comm, ctypes.c_char_p(blob)))
+
+
+def comm_reset(comm, stream=None):
+    check(lib().krt_comm_reset(comm, _stream(stream)))
 
 
 def comm_destroy(comm):

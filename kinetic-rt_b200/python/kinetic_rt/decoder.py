@@ -263,9 +263,24 @@ class PagedDecoder:
             self.layer(li)
         self.tail()
 
-    def capture(self):
-        """The step as a CUDA graph (warm-up on a side stream first)."""
+    def capture(self, warm=True):
+        """The step as a CUDA graph.  With `warm`, one eager step runs first on a
+        side stream (every entry point's first-call set-up happens outside the
+        capture) and the state it advanced is put back: the hidden state,
+        positions and lengths are restored, and the K/V it wrote at the
+        current positions are rewritten identically by the next step."""
         torch = self.torch
+        if warm:
+            saved = [t.clone() for t in (self.h, self.positions, self.seq_lens, self.tokens, self.next_input)]
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.step()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            for t, v in zip((self.h, self.positions, self.seq_lens, self.tokens, self.next_input), saved):
+                t.copy_(v)
+            torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self.step()

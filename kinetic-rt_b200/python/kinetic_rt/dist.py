@@ -33,6 +33,17 @@ class TPComm:
     def allreduce(self, send, recv, status, stream=None):
         _lib.allreduce(self.handle, send, recv, status, stream)
 
+    def reset(self, group=None, stream=None):
+        """Re-agree the exchange state after a peer wait ran out (status bit
+        16): every rank drains its stream, zeroes its exchange areas
+        (krt_comm_reset) and meets the others at a barrier."""
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # no rank's kernel still writes into a peer's buffer
+        _lib.comm_reset(self.handle, stream)
+        dist.barrier(group=group)  # no rank starts a collective before every buffer is clear
+
     def close(self):
         if self.handle:
             _lib.comm_destroy(self.handle)

@@ -141,30 +141,27 @@ def tiny_model(rng, L=2, D=256, H=4, KV=2, I=384, V=1000):
     return shape, full
 
 
-def test_decode_steps_match_oracle(torch_cuda):
-    """Three graph-replayed decode steps of a 2-layer model, 5 sequences at
-    ragged positions, against the oracle step by step (the oracle's token is
-    fed back on both sides, so a near-tie cannot make the runs diverge)."""
-    torch = torch_cuda
+def run_decoder_against_oracle(torch, rank=0, world=1, comm=None, steps=3):
     from python.kinetic_rt.decoder import PagedDecoder, RankWeights
     rng = np.random.Generator(np.random.PCG64(4))
     shape, full = tiny_model(rng)
     B, max_len = 5, 80
-    w = RankWeights.from_full(torch, shape, full, 0, 1)
-    dec = PagedDecoder(torch, shape, w, B, max_len)
+    w = RankWeights.from_full(torch, shape, full, rank, world)
+    dec = PagedDecoder(torch, shape, w, B, max_len, comm=comm, rank=rank, world=world)
     start_pos = np.array([0, 5, 16, 33, 70])
     start_tok = rng.integers(0, shape.vocab, size=B)
-    # prefix K/V: random bf16 values in both the oracle's pools and the device's
+    # prefix K/V: random bf16 values in the oracle's pools; each rank holds its KV heads
     pools = [bf(rng, dec.num_blocks, 16, 2, shape.n_kv_heads, 128) for _ in range(shape.n_layers)]
+    hk = shape.n_kv_heads // world
     for p, pd in zip(pools, dec.pools):
-        pd.copy_(dev(torch, p.reshape(dec.num_blocks, 16, -1)))
+        pd.copy_(dev(torch, np.ascontiguousarray(p[:, :, :, rank * hk:(rank + 1) * hk]).reshape(dec.num_blocks, 16, -1)))
     dec.start(start_tok, start_pos)
     table = dec.block_table.cpu().numpy()
     cos, sin = fused_layer.rope_tables(np.arange(max_len), 128, shape.rope_theta)
     graph = dec.capture()
     h = full["embed"][start_tok]
     pos = start_pos.copy()
-    for step in range(3):
+    for step in range(steps):
         logits, tok, h_next = odec.decode_step(full, h, pos, table, pools, cos, sin, shape.n_heads,
                                                shape.n_kv_heads, 16)
         dec.next_input.copy_(torch.from_numpy(tok.astype(np.int32)))
@@ -174,11 +171,55 @@ def test_decode_steps_match_oracle(torch_cuda):
         top2 = np.sort(logits, -1)[:, -2:]
         near_tie = top2[:, 1] - top2[:, 0] < ATOL + RTOL * np.abs(top2[:, 1])
         assert np.all((got_tok == tok) | near_tie), (step, got_tok, tok)
-        for li in range(shape.n_layers):  # the step's K/V landed at each sequence's slot
-            got_pool = dec.pools[li].float().cpu().numpy().reshape(pools[li].shape)
+        for li in range(shape.n_layers):  # the step's K/V (this rank's heads) landed at each sequence's slot
+            got_pool = dec.pools[li].float().cpu().numpy().reshape(dec.num_blocks, 16, 2, hk, 128)
             for s in range(B):
                 blk, off = table[s][pos[s] // 16], pos[s] % 16
-                np.testing.assert_allclose(got_pool[blk, off], pools[li][blk, off], atol=ATOL, rtol=RTOL)
+                np.testing.assert_allclose(got_pool[blk, off], pools[li][blk, off, :, rank * hk:(rank + 1) * hk],
+                                           atol=ATOL, rtol=RTOL)
         np.testing.assert_array_equal(dec.h.float().cpu().numpy(), h_next)
         assert dec.positions.cpu().numpy().tolist() == (pos + 1).tolist()
         h, pos = h_next, pos + 1
+    del graph
+    return dec
+
+
+def _tp_decoder_worker(rank, world, port):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from python.kinetic_rt.dist import TPComm
+    comm = TPComm(rank, world, max_n_out=256)
+    try:
+        run_decoder_against_oracle(torch, rank, world, comm)
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_decode_steps_tensor_parallel_match_oracle(torch_cuda):
+    """The same three steps with the model split over two GPUs (heads,
+    intermediate features and vocabulary; fused allreduce and the greedy
+    exchange over NVLink): both ranks match the oracle."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_tp_decoder_worker, args=(2, port), nprocs=2, join=True)
+
+
+def test_decode_steps_match_oracle(torch_cuda):
+    """Three graph-replayed decode steps of a 2-layer model, 5 sequences at
+    ragged positions, against the oracle step by step (the oracle's token is
+    fed back on both sides, so a near-tie cannot make the runs diverge)."""
+    run_decoder_against_oracle(torch_cuda)

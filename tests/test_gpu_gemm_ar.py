@@ -132,3 +132,58 @@ def test_gemm_ar_multi_gpu(torch_cuda, world):
     import torch.multiprocessing as mp
     cases = [(1, 4096, 4096), (64, 14336, 4096), (300, 4096, 4096)]
     mp.spawn(_tp_worker, args=(world, _free_port(), cases), nprocs=world, join=True)
+
+
+def _timeout_worker(rank, world, port):
+    """Rank 1 skips one fused call (between steps, nothing in flight); rank 0's
+    bounded peer wait runs out and reports status bit 16; both ranks reset the
+    communicator (drain, barrier, krt_comm_reset, barrier); the next call
+    matches the fp32 product on both ranks."""
+    import datetime
+    import time
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from python.kinetic_rt import _lib
+    from python.kinetic_rt.dist import TPComm
+    comm = TPComm(rank, world, max_n_out=4096)
+    ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    try:
+        T, K, N = 64, 4096, 4096
+        x, w = make_case(T, K, N, seed=55)
+        lo, hi = orc.chunk_bounds(K, world)[rank]
+        xd, wd = to_dev(torch, x[:, lo:hi]), to_dev(torch, w[:, lo:hi])
+        y = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+        ref = orc.rowparallel_reference(bf16_bits_to_f32(x), bf16_bits_to_f32(w))
+        comm.gemm_ar(xd, wd, y, ws)  # a good call first
+        assert _lib.read_status(ws) == (0, 0)
+        dist.barrier()
+        t0 = time.time()
+        if rank == 0:
+            comm.gemm_ar(xd, wd, y, ws)  # its peer never joins this one
+            rc, bits = _lib.read_status(ws)
+            elapsed = time.time() - t0
+            assert rc == _lib.KRT_ERR_DEVICE and bits & 16, bits
+            assert elapsed < 6.0, elapsed
+        comm.reset()
+        y.fill_(0)
+        comm.gemm_ar(xd, wd, y, ws)
+        rc, bits = _lib.read_status(ws)
+        assert rc == 0 and bits == 0, f"rank {rank} status {bits:#x} after the reset"
+        np.testing.assert_allclose(y.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_gemm_ar_peer_timeout_then_reset(torch_cuda):
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.spawn(_timeout_worker, args=(2, _free_port()), nprocs=2, join=True)
