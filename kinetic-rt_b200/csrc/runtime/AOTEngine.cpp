@@ -157,15 +157,28 @@ void AOTEngine::compile_ahead_of_time(const std::string& output_filepath, uintpt
                                       const std::string& kinetic_target) {
   (void)stream_ptr;
   std::lock_guard<std::recursive_mutex> lock(mutex_);
-  const std::string path = kernel_dir() + "/fused_rmsnorm_qkv_rope.sm_100a.cubin";
-  std::ifstream in(path, std::ios::binary);
-  if (!in) throw std::runtime_error("AOT compilation failed: kernel image not found at " + path);
-  std::vector<uint8_t> binary((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+  std::vector<uint8_t> binary;
 #if defined(KRT_MOCK_CUDA)
   const char* kind = "mock";
+  const bool cuda_target = kinetic_target.rfind("CUDA", 0) == 0 || kinetic_target.find("sm") != std::string::npos;
+  if (!cuda_target) {
+    // Host-only build, non-CUDA target (a headless test host's "CPU_CPU"): a
+    // structurally valid 64-bit ELF header for the other backend, as the
+    // reference's mock compile emits (python/kinetic_rt/fusion_forge.py:508-537)
+    binary.assign(64, 0);
+    binary[0] = 0x7f, binary[1] = 'E', binary[2] = 'L', binary[3] = 'F';
+    binary[4] = 2, binary[5] = 1, binary[6] = 1;
+    binary[18] = 0xE0;  // EM_AMDGPU
+  }
 #else
   const char* kind = "production";
 #endif
+  if (binary.empty()) {
+    const std::string path = kernel_dir() + "/fused_rmsnorm_qkv_rope.sm_100a.cubin";
+    std::ifstream in(path, std::ios::binary);
+    if (!in) throw std::runtime_error("AOT compilation failed: kernel image not found at " + path);
+    binary.assign((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+  }
   const std::string meta = std::string("{\"target\": \"") + kinetic_target +
                            "\", \"kernels\": [\"fused_rmsnorm_qkv_rope\", \"fused_rmsnorm_qkv_rope_bf16\"], "
                            "\"version\": 1, \"artifact_kind\": \"" + kind + "\"}";
