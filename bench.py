@@ -40,6 +40,9 @@ BATCH, CTX, BLOCK = 64, 2048, 16              # --workload layer
 STACK_BATCH, PROMPT, GEN_STEPS = 128, 4096, 256  # --workload stack
 L2_BYTES = 126 * 1024 * 1024
 NVLINK_GBS = 770.0  # measured B200 peer-copy bandwidth per direction over NVLink 5 (900 GB/s nominal)
+# allreduce messages (bf16 bytes) from which the NCCL route is taken: set from
+# the fused-vs-NCCL sweep (--workload gemm_ar) on B200
+NCCL_THRESHOLD = 1 << 62
 
 
 def peaks():
@@ -611,6 +614,115 @@ def tp_parity_check(torch, comm, rank, world):
             "tolerance": "max-abs 2e-2 + rel 1e-2 vs unsharded fp32"}
 
 
+GEMM_AR_TOKENS = (1, 8, 64, 512, 4096, 8192)
+
+
+def gemm_ar_sweep(torch, comm, rank, world, tokens=GEMM_AR_TOKENS, reps=5):
+    """Config 3: o_proj (K = 4096) and down_proj (K = 14336) row-parallel GEMM +
+    allreduce at TP = world for each token count, through the fused exchange
+    and through the NCCL route (GEMM, then ncclAllReduce), both timed on the
+    device (max over ranks) and checked against the unsharded fp32 product
+    (torch on this GPU) and for bit-identity across ranks.  roofline_us =
+    max(HBM bytes / HBM peak, FLOPs / bf16 peak, allreduce bus bytes / NVLink
+    peak) with bus bytes 2 (N-1)/N x T x 4096 x 2 (a bf16 ring)."""
+    import torch.distributed as dist
+    from python.kinetic_rt import _lib
+    hbm, _ = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tflops = 1590.0
+    ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    rows = []
+    for name, K in (("o_proj", HIDDEN), ("down_proj", INTER)):
+        kr = K // world
+        g = torch.Generator(device="cuda").manual_seed(K)
+        w_full = (torch.randn(HIDDEN, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        w = w_full[:, rank * kr:(rank + 1) * kr].contiguous()
+        for T in tokens:
+            gx = torch.Generator(device="cuda").manual_seed(T * 7 + K)
+            x_full = torch.randn(T, K, generator=gx, device="cuda").to(torch.bfloat16)
+            x = x_full[:, rank * kr:(rank + 1) * kr].contiguous()
+            ref = x_full.float() @ w_full.float().t()
+            y = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
+            args = _lib.gemm_ar_args(x, w, y, ws)
+            row = {"proj": name, "tokens": T, "tp": world}
+            for route in ("fused", "nccl"):
+                if route == "nccl" and (world == 1 or not getattr(comm, "has_nccl", False)):
+                    continue
+                if comm is not None and getattr(comm, "has_nccl", False):
+                    comm.set_nccl_threshold(0 if route == "nccl" else (1 << 62))
+                call = lambda: _lib.rowparallel_gemm_ar(comm.handle if comm is not None else None, args)
+                call()
+                torch.cuda.synchronize()
+                rc, bits = _lib.read_status(ws)
+                err = (y.float() - ref).abs()
+                ok = rc == 0 and bool((err <= 2e-2 + 1e-2 * ref.abs()).all())
+                same = True
+                if world > 1:
+                    allv = [torch.empty_like(y) for _ in range(world)]
+                    dist.all_gather(allv, y)
+                    same = all(torch.equal(a.view(torch.int16), allv[0].view(torch.int16)) for a in allv)
+                barrier(torch, world)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    call()
+                e1.record()
+                barrier(torch, world)
+                us = max_over_ranks(torch, e0.elapsed_time(e1), world) * 1e3 / reps
+                row[f"{route}_us"] = round(us, 2)
+                row[f"{route}_max_abs"] = round(float(err.max()), 4)
+                row[f"{route}_ok"] = ok and same
+            nbytes = HIDDEN * kr * 2 + T * kr * 2 + T * HIDDEN * 2
+            flops = 2.0 * T * kr * HIDDEN
+            bus = 2 * (world - 1) / world * T * HIDDEN * 2
+            target = max(nbytes / hbm / 1e3, flops / tflops / 1e6, bus / NVLINK_GBS / 1e3)
+            best = min(row.get("fused_us", 1e30), row.get("nccl_us", 1e30))
+            row.update({"roofline_us": round(target, 3), "bound": ("hbm" if target == nbytes / hbm / 1e3 else
+                                                                  "tensor" if target == flops / tflops / 1e6 else
+                                                                  "nvlink"),
+                        "best_route": "fused" if row.get("fused_us", 1e30) <= row.get("nccl_us", 1e30) else "nccl",
+                        "frac_of_roofline": round(target / best, 4)})
+            rows.append(row)
+    if comm is not None and getattr(comm, "has_nccl", False):
+        comm.set_nccl_threshold(comm.nccl_threshold)
+    return rows
+
+
+def run_gemm_ar(args, rank, world, local_rank):
+    """--workload gemm_ar: the config-3 sweep alone, one JSON line."""
+    import torch
+    torch.cuda.set_device(local_rank)
+    comm = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=120))
+        from python.kinetic_rt.dist import TPComm
+        comm = TPComm(rank, world, max_n_out=HIDDEN)
+        comm.attach_nccl(NCCL_THRESHOLD)
+    rows = gemm_ar_sweep(torch, comm, rank, world)
+    if rank == 0:
+        worst = min(r["frac_of_roofline"] for r in rows)
+        print(json.dumps({
+            "metric": "row-parallel GEMM + allreduce, % of roofline (config 3)", "value": worst,
+            "unit": "min frac_of_roofline over rows", "n_gpus": world, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (N(0,1) activations, N(0,0.02) weights)", "scaling": "strong",
+            "config": {"workload": f"o_proj [4096->4096] and down_proj [14336->4096], K sharded over TP={world}, "
+                                   f"tokens {list(GEMM_AR_TOKENS)}"},
+            "rows": rows, "all_ok": all(r.get("fused_ok", True) and r.get("nccl_ok", True) for r in rows)}),
+            flush=True)
+    if comm is not None:
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def stack_kernel_bytes(world, ctx):
     """Algorithmic bytes per launch of each kernel of the decode step (this
     rank's share): every input read once, every output written once."""
@@ -643,8 +755,10 @@ def run_stack(args, rank, world, local_rank):
                                 timeout=datetime.timedelta(seconds=120))
         from python.kinetic_rt.dist import TPComm
         comm = TPComm(rank, world, max_n_out=HIDDEN)
+        comm.attach_nccl(NCCL_THRESHOLD)
     from python.kinetic_rt.decoder import LLAMA3_8B, PagedDecoder, RankWeights
     parity = tp_parity_check(torch, comm, rank, world)
+    config3 = gemm_ar_sweep(torch, comm, rank, world) if world > 1 else None
     K, W = args.steps, args.warmup
     B = STACK_BATCH
     # the position the first warm-up step processes: the timed steps sit in
@@ -788,12 +902,14 @@ def run_stack(args, rank, world, local_rank):
                      "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4), "context_mid": ctx_mid},
             "kernels": klist + ([prefill] if prefill else []),
             "parity": parity,
+            "config3_gemm_ar": config3,
             "cpu_baseline": base if base else {"value": None, "note": "timed at N=1 only (rank 0 alone on the host)"},
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
     bad = not (parity["within_tolerance"] and parity["ranks_identical"] and parity.get("step_tokens_identical", True)
-               and parity.get("step_hidden_identical", True))
+               and parity.get("step_hidden_identical", True)
+               and all(r.get("fused_ok", True) and r.get("nccl_ok", True) for r in (config3 or [])))
     if comm is not None:
         import torch.distributed as dist
         torch.cuda.synchronize()
@@ -1022,7 +1138,7 @@ def main():
                     help="timed steps (default: 64 decode steps of the stack, 20000 layer steps)")
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["krt", "reference"], default="krt")
-    ap.add_argument("--workload", choices=["stack", "layer", "prefill"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "layer", "prefill", "gemm_ar"], default="stack",
                     help="stack: decode steps of the Llama-3-8B-shaped stack (default); layer: one decoder layer's "
                          "hot path; prefill: the fused QKV prefill kernel alone")
     args = ap.parse_args()
@@ -1043,6 +1159,8 @@ def main():
         run_prefill(args, rank, world, local_rank)
     elif args.workload == "layer":
         run_krt(args, rank, world, local_rank)
+    elif args.workload == "gemm_ar":
+        run_gemm_ar(args, rank, world, local_rank)
     else:
         run_stack(args, rank, world, local_rank)
 

@@ -212,6 +212,25 @@ KRT_API int krt_comm_ipc_handle(krt_comm* comm, void* handle_out);
 KRT_API int krt_comm_open_peers(krt_comm* comm, const void* handles);
 KRT_API int krt_comm_destroy(krt_comm* comm);
 
+/* NCCL for large messages (the reference's intended backend,
+ * src/Communicator.cpp:10-27, whose ncclAllReduce call it left commented
+ * out).  libnccl.so.2 is loaded at run time on first use (the copy already in
+ * the process, else the system's); nothing else in the library needs it.
+ *   krt_nccl_unique_id    one rank creates the id (krt_nccl_id_size bytes) and
+ *                         shares it with the others out of band
+ *   krt_comm_attach_nccl  collective: ncclCommInitRank for this communicator's
+ *                         rank and world; afterwards krt_allreduce of at least
+ *                         threshold_bytes, and krt_rowparallel_gemm_ar whose
+ *                         bf16 output (num_tokens * n_out * 2 bytes, dense rows)
+ *                         is at least that large, run the GEMM without the
+ *                         fused exchange followed by one ncclAllReduce in place
+ *                         (sum in NCCL's bf16 arithmetic).  SIZE_MAX disables it
+ *                         again; calling it twice only changes the threshold.
+ * krt_comm_destroy also destroys the NCCL communicator. */
+KRT_API size_t krt_nccl_id_size(void);
+KRT_API int krt_nccl_unique_id(void* id_out);
+KRT_API int krt_comm_attach_nccl(krt_comm* comm, const void* id, size_t threshold_bytes);
+
 /* Recovery after a peer wait ran out (status bit 16), e.g. when one rank
  * skipped or lost a collective call: the exchange epochs of the ranks no
  * longer agree, and every later fused call would wait out its budget.

@@ -14,7 +14,11 @@
 // every rank pushes its slice o to o, o sums in rank order and pushes the
 // result to everyone.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
+#include <climits>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -35,7 +39,43 @@ struct krt_comm {
   char* local = nullptr;
   char* peer[krt::kMaxWorld] = {};
   bool peers_open = false;
+  ncclComm_t nccl = nullptr;      // krt_comm_attach_nccl
+  size_t nccl_threshold = SIZE_MAX;  // messages of at least this many bytes go through NCCL
 };
+
+namespace {
+// NCCL, resolved at run time from libnccl.so.2 (the copy the process already
+// loaded, e.g. torch's, or the system's): only its header is used at build
+// time, so the library links no NCCL and runs without one until a caller
+// attaches an NCCL communicator.
+struct NcclApi {
+  bool ok = false;
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclCommDestroy) comm_destroy = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+};
+const NcclApi& nccl_api() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+  });
+  return api;
+}
+int nccl_error(ncclResult_t r, const char* what) {
+  return krt::set_error(KRT_ERR_CUDA, "%s: NCCL error %d (%s)", what, (int)r,
+                        nccl_api().error_string ? nccl_api().error_string(r) : "?");
+}
+}  // namespace
 
 namespace krt {
 
@@ -317,8 +357,38 @@ extern "C" int krt_comm_reset(krt_comm* c, void* stream) {
   return clear_error();
 }
 
+extern "C" size_t krt_nccl_id_size(void) { return sizeof(ncclUniqueId); }
+
+extern "C" int krt_nccl_unique_id(void* id_out) {
+  if (!id_out) return set_error(KRT_ERR_INVALID, "krt_nccl_unique_id: NULL argument");
+  const NcclApi& api = nccl_api();
+  if (!api.ok) return set_error(KRT_ERR_UNSUPPORTED, "krt_nccl_unique_id: libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  ncclResult_t r = api.get_unique_id(&id);
+  if (r != ncclSuccess) return nccl_error(r, "krt_nccl_unique_id");
+  std::memcpy(id_out, &id, sizeof(id));
+  return clear_error();
+}
+
+extern "C" int krt_comm_attach_nccl(krt_comm* c, const void* id, size_t threshold_bytes) {
+  if (!c || !id) return set_error(KRT_ERR_INVALID, "krt_comm_attach_nccl: NULL argument");
+  const NcclApi& api = nccl_api();
+  if (!api.ok) return set_error(KRT_ERR_UNSUPPORTED, "krt_comm_attach_nccl: libnccl.so.2 could not be loaded");
+  if (!c->nccl) {
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclComm_t nc = nullptr;
+    ncclResult_t r = api.comm_init_rank(&nc, c->world, uid, c->rank);
+    if (r != ncclSuccess) return nccl_error(r, "krt_comm_attach_nccl: ncclCommInitRank");
+    c->nccl = nc;
+  }
+  c->nccl_threshold = threshold_bytes;
+  return clear_error();
+}
+
 extern "C" int krt_comm_destroy(krt_comm* c) {
   if (!c) return clear_error();
+  if (c->nccl && nccl_api().ok) nccl_api().comm_destroy(c->nccl);
   for (int q = 0; q < c->world; ++q)
     if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
   if (c->local) cudaFree(c->local);
@@ -349,6 +419,12 @@ extern "C" int krt_allreduce(krt_comm* c, const void* send, void* recv, size_t c
   if (dtype != KRT_DTYPE_FLOAT32 && dtype != KRT_DTYPE_BFLOAT16)
     return set_error(KRT_ERR_UNSUPPORTED, "krt_allreduce: float32 and bfloat16 only");
   const size_t esize = dtype == KRT_DTYPE_FLOAT32 ? 4 : 2;
+  if (c->nccl && count * esize >= c->nccl_threshold) {
+    ncclResult_t r = nccl_api().all_reduce(send, recv, count, dtype == KRT_DTYPE_FLOAT32 ? ncclFloat32 : ncclBfloat16,
+                                           ncclSum, c->nccl, (cudaStream_t)stream);
+    if (r != ncclSuccess) return nccl_error(r, "krt_allreduce: ncclAllReduce");
+    return clear_error();
+  }
   // Elements per launch: staging holds world rows of (slice + count) floats,
   // the result area holds count elements.
   const size_t stg_bytes = v.L.result_off - v.L.staging_off;
@@ -476,7 +552,13 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
                      a->workspace_bytes, (size_t)kWsHeaderBytes);
   GemmArParams p;
   std::memset(&p, 0, sizeof(p));
-  if (c) {
+  // Large outputs with an NCCL communicator attached: the GEMM runs without
+  // the fused exchange (its partial lands in y, comm rank 0 adding the
+  // residual, so the sum holds it once) and one in-place ncclAllReduce of y
+  // follows.  Every rank takes the same route (same sizes, same threshold).
+  const bool via_nccl = c && c->world > 1 && c->nccl && a->y_stride == a->n_out &&
+                        (size_t)a->num_tokens * a->n_out * 2 >= c->nccl_threshold;
+  if (c && !via_nccl) {
     int rc = comm_view(c, &p.comm);
     if (rc) return rc;
     if (a->n_out > c->max_n)
@@ -486,6 +568,7 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     p.comm.world = 1;
     p.comm.rank = 0;
   }
+  const void* residual = via_nccl && c->rank != 0 ? nullptr : a->residual;
   const int num_kb = a->k_local / 64;
   p.n_out = a->n_out;
   p.k_local = a->k_local;
@@ -524,7 +607,7 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
     sl.p.tmem_cols = cols;
     sl.p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
     sl.p.residual =
-        a->residual ? static_cast<const __nv_bfloat16*>(a->residual) + (size_t)t0 * a->y_stride : nullptr;
+        residual ? static_cast<const __nv_bfloat16*>(residual) + (size_t)t0 * a->y_stride : nullptr;
     const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
     int rc = make_tmap_bf16_3d(&sl.tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local,
                                (uint64_t)a->k_local, (uint32_t)sl.cfg.tile_m, (uint32_t)sl.p.kc);
@@ -537,6 +620,11 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
   for (const Slice& sl : slices) {
     cudaError_t e = launch_rowparallel_gemm_ar(sl.cfg.tile_m, sl.tmap_w, sl.tmap_x, sl.p, sl.cfg.tiles, s);
     if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
+  }
+  if (via_nccl) {
+    ncclResult_t r = nccl_api().all_reduce(a->y, a->y, (size_t)a->num_tokens * a->n_out, ncclBfloat16, ncclSum,
+                                           c->nccl, s);
+    if (r != ncclSuccess) return nccl_error(r, "krt_rowparallel_gemm_ar: ncclAllReduce");
   }
   return clear_error();
 }

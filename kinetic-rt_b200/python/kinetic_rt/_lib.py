@@ -120,6 +120,9 @@ SIGNATURES = {
     "krt_comm_open_peers": (ctypes.c_int, [_vp, _vp]),
     "krt_comm_destroy": (ctypes.c_int, [_vp]),
     "krt_comm_reset": (ctypes.c_int, [_vp, _vp]),
+    "krt_nccl_id_size": (ctypes.c_size_t, []),
+    "krt_nccl_unique_id": (ctypes.c_int, [_vp]),
+    "krt_comm_attach_nccl": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t]),
     "krt_allreduce": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t, _i32, _vp, _vp]),
     "krt_rowparallel_gemm_ar_workspace_size": (ctypes.c_size_t, []),
     "krt_rowparallel_gemm_ar": (ctypes.c_int, [_vp, ctypes.POINTER(GemmArArgs), _vp]),
@@ -267,6 +270,17 @@ def comm_ipc_handle(comm):
 def comm_open_peers(comm, handles):
     blob = b"".join(handles)
     check(lib().krt_comm_open_peers(comm, ctypes.c_char_p(blob)))
+
+
+def nccl_unique_id():
+    n = int(lib().krt_nccl_id_size())
+    buf = ctypes.create_string_buffer(n)
+    check(lib().krt_nccl_unique_id(buf))
+    return buf.raw
+
+
+def comm_attach_nccl(comm, nccl_id, threshold_bytes):
+    check(lib().krt_comm_attach_nccl(comm, ctypes.c_char_p(nccl_id), ctypes.c_size_t(int(threshold_bytes))))
 
 
 def comm_reset(comm, stream=None):

@@ -21,6 +21,7 @@ def exchange_handles(handle, group=None):
 class TPComm:
     def __init__(self, rank, world_size, max_n_out, group=None):
         self.rank, self.world_size = int(rank), int(world_size)
+        self.has_nccl, self.nccl_threshold = False, None
         self.handle = _lib.comm_create(self.rank, self.world_size, max_n_out)
         if self.world_size > 1:
             mine = _lib.comm_ipc_handle(self.handle)
@@ -32,6 +33,21 @@ class TPComm:
 
     def allreduce(self, send, recv, status, stream=None):
         _lib.allreduce(self.handle, send, recv, status, stream)
+
+    def attach_nccl(self, threshold_bytes, group=None):
+        """An NCCL communicator beside the peer buffers (rank 0 makes the id,
+        every rank joins); messages of at least threshold_bytes use it."""
+        import torch.distributed as dist
+        nid = _lib.nccl_unique_id() if self.rank == 0 else None
+        ids = [None] * dist.get_world_size(group)
+        dist.all_gather_object(ids, nid, group=group)
+        _lib.comm_attach_nccl(self.handle, ids[0], threshold_bytes)
+        self.has_nccl, self.nccl_threshold = True, int(threshold_bytes)
+
+    def set_nccl_threshold(self, threshold_bytes):
+        """Changes the threshold of an attached NCCL communicator (every rank
+        must use the same value)."""
+        _lib.comm_attach_nccl(self.handle, b"\0" * 128, min(int(threshold_bytes), (1 << 64) - 1))
 
     def reset(self, group=None, stream=None):
         """Re-agree the exchange state after a peer wait ran out (status bit

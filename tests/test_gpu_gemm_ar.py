@@ -187,3 +187,60 @@ def test_gemm_ar_peer_timeout_then_reset(torch_cuda):
     import torch.multiprocessing as mp
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     mp.spawn(_timeout_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _nccl_worker(rank, world, port):
+    """The size-selected NCCL route (threshold 0: every call): GEMM without the
+    fused exchange, then ncclAllReduce in place; with a residual (added once,
+    by rank 0) and without; plus krt_allreduce through NCCL."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from python.kinetic_rt import _lib
+    from python.kinetic_rt.dist import TPComm
+    comm = TPComm(rank, world, max_n_out=4096)
+    comm.attach_nccl(0)
+    ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    try:
+        for (T, K, N, with_res) in [(1, 4096, 4096, False), (64, 14336, 4096, True), (300, 4096, 4096, True),
+                                    (512, 1792 * world, 4096, False)]:
+            x, w = make_case(T, K, N, seed=2000 + T + K)
+            rng = np.random.Generator(np.random.PCG64(T))
+            res = f32_to_bf16_bits(rng.standard_normal((T, N), dtype=np.float32))
+            lo, hi = orc.chunk_bounds(K, world)[rank]
+            xd, wd = to_dev(torch, x[:, lo:hi]), to_dev(torch, w[:, lo:hi])
+            y = to_dev(torch, res) if with_res else torch.full((T, N), 7.0, dtype=torch.bfloat16, device="cuda")
+            comm.gemm_ar(xd, wd, y, ws) if not with_res else _lib.rowparallel_gemm_ar(
+                comm.handle, _lib.gemm_ar_args(xd, wd, y, ws, residual=y))
+            rc, bits = _lib.read_status(ws)
+            assert rc == 0 and bits == 0
+            ref = orc.rowparallel_reference(bf16_bits_to_f32(x), bf16_bits_to_f32(w))
+            if with_res:
+                ref = ref + bf16_bits_to_f32(res)
+            np.testing.assert_allclose(y.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+            all_y = [None] * world
+            dist.all_gather_object(all_y, y.view(torch.int16).cpu().numpy())
+            for other in all_y:
+                assert np.array_equal(other, all_y[0]), "ranks disagree"
+        send = torch.full((1000,), float(rank + 1), device="cuda")
+        recv = torch.zeros_like(send)
+        comm.allreduce(send, recv, ws)
+        torch.cuda.synchronize()
+        assert torch.all(recv == float(sum(range(1, world + 1)))).item()
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_gemm_ar_nccl_route(torch_cuda, world):
+    torch = torch_cuda
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mp.spawn(_nccl_worker, args=(world, _free_port()), nprocs=world, join=True)
