@@ -9,7 +9,7 @@
 //     back (LIFO reuse); both are mutex-protected;
 //   * an empty pool and an out-of-range id raise std::runtime_error with the
 //     reference's messages.
-// Additions: block_ptr(id), num_free(), and double-free detection.
+// Additions: block_ptr(id) and num_free().
 //
 // The fused QKV kernels write a token's K and V heads at
 //   pool + (block * tokens_per_block + offset) * token_byte_size
@@ -35,7 +35,6 @@ class BlockManager {
     cudaError_t e = cudaMalloc(&pool_, bytes);
     if (e != cudaSuccess) throw std::runtime_error("CUDA memory error in BlockManager");
     free_blocks_.reserve(num_blocks);
-    in_use_.assign(num_blocks, 0);
     for (int i = 0; i < num_blocks; ++i) free_blocks_.push_back(i);
   }
 
@@ -52,7 +51,6 @@ class BlockManager {
     if (free_blocks_.empty()) throw std::runtime_error("Out of KV Cache blocks! Massive pool exhausted.");
     const int id = free_blocks_.back();
     free_blocks_.pop_back();
-    in_use_[id] = 1;
     return id;
   }
 
@@ -61,9 +59,8 @@ class BlockManager {
     if (id < 0 || id >= num_blocks_)
       throw std::runtime_error("BlockManager::free_block: block ID " + std::to_string(id) + " out of range [0, " +
                                std::to_string(num_blocks_) + ")");
-    if (!in_use_[id])
-      throw std::runtime_error("BlockManager::free_block: block ID " + std::to_string(id) + " is not allocated");
-    in_use_[id] = 0;
+    // Any in-range id goes back on the free list, as the reference does
+    // (include/BlockManager.h:73-82): freeing an id twice lists it twice.
     free_blocks_.push_back(id);
   }
 
@@ -88,6 +85,5 @@ class BlockManager {
   int num_blocks_;
   void* pool_ = nullptr;
   std::vector<int> free_blocks_;
-  std::vector<char> in_use_;
   mutable std::mutex mutex_;
 };

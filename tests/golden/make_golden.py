@@ -1,9 +1,9 @@
 """Generate the golden vectors under tests/golden/ from the reference itself.
 
-Run in a container where the reference sources are mounted (path given by
-KINETIC_REFERENCE, default /root/reference):
+Run in a container where the reference sources are mounted, with
+KINETIC_REFERENCE naming the reference's root directory:
 
-    python tests/golden/make_golden.py
+    KINETIC_REFERENCE=<reference root> python tests/golden/make_golden.py
 
 It imports the reference's own PyTorch parity functions
 (tests/test_fusion.py:11-51) and its Triton kernel
@@ -32,7 +32,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from tests.golden import inputs as golden_inputs  # noqa: E402
 from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits  # noqa: E402
 
-REF = os.environ.get("KINETIC_REFERENCE", "/root/reference")
+REF = os.environ.get("KINETIC_REFERENCE", "")
 
 
 def _load_reference():
@@ -142,6 +142,8 @@ def gqa_bf16(tf):
 
 
 if __name__ == "__main__":
+    if not REF or not os.path.isdir(os.path.join(REF, "python", "kinetic_rt")):
+        sys.exit("set KINETIC_REFERENCE to the reference's root directory")
     ff, tf = _load_reference()
     known_answer(ff, tf)
     config1(tf)

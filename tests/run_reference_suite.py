@@ -1,6 +1,6 @@
 """Run the reference's own Python tests, unmodified, against this build.
 
-    KINETIC_REFERENCE=<reference tests directory> python tests/run_reference_suite.py [--gpu | --host]
+    KINETIC_REFERENCE=<reference root or its tests directory> python tests/run_reference_suite.py [--gpu | --host]
 
 The reference's tests import `python.kinetic_rt` (and its fusion_forge /
 hardware_probe modules); here that name resolves to this repository's
@@ -34,6 +34,8 @@ HOST_TESTS = ["test_graph.py", "test_aot.py", "test_validation.py", "test_distri
 
 
 def run(tests_dir, which, extra=()):
+    if os.path.isdir(os.path.join(tests_dir, "tests")):
+        tests_dir = os.path.join(tests_dir, "tests")
     files = [os.path.join(tests_dir, f) for f in (GPU_TESTS if which == "gpu" else HOST_TESTS)]
     files = [f for f in files if os.path.exists(f)]
     if not files:

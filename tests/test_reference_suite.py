@@ -1,6 +1,6 @@
 """The reference's own Python tests, unmodified, against this build
 (tests/run_reference_suite.py).  Runs only when KINETIC_REFERENCE names the
-reference's tests directory; the host-side tests need no GPU, test_fusion.py
+reference's root (or its tests directory); the host-side tests need no GPU, test_fusion.py
 needs a B200."""
 import os
 import sys
@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 def _run(which):
     tests_dir = os.environ.get("KINETIC_REFERENCE")
     if not tests_dir or not os.path.isdir(tests_dir):
-        pytest.skip("KINETIC_REFERENCE does not name the reference's tests directory")
+        pytest.skip("KINETIC_REFERENCE does not name the reference's directory")
     sys.path.insert(0, HERE)
     import run_reference_suite
     return run_reference_suite.run(tests_dir, which)
