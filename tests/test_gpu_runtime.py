@@ -194,3 +194,58 @@ def test_communicator_world_one(torch_cuda, kinetic_rt):
     assert c.read_status(torch.cuda.current_stream().cuda_stream) == 0
     ref = orc.rowparallel_reference(bf16_bits_to_f32(x), bf16_bits_to_f32(w))
     np.testing.assert_allclose(y.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
+def _core_comm_worker(rank, world, port):
+    """python.kinetic_rt.Communicator(rank, world) as the reference constructs
+    it (include/Communicator.h:15-26), one process per GPU: the peers' buffers
+    are mapped with ipc_handle() / open_peers() (handles exchanged here over
+    gloo), then all_reduce_async sums 1.0 + 2.0 (tests/test_distributed.py:47-48)
+    and the fused row-parallel GEMM + allreduce matches the fp32 product."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    import python.kinetic_rt as k
+    c = k.Communicator(rank, world)
+    handles = [None] * world
+    dist.all_gather_object(handles, c.ipc_handle())
+    c.open_peers(handles)
+    stream = torch.cuda.current_stream().cuda_stream
+    count = 100
+    send = torch.full((count,), float(rank + 1), dtype=torch.float32, device="cuda")
+    recv = torch.zeros_like(send)
+    c.all_reduce_async(send.data_ptr(), recv.data_ptr(), count, 0, 0, stream)
+    torch.cuda.synchronize()
+    assert torch.all(recv == 3.0).item()
+    rng = np.random.Generator(np.random.PCG64(62))
+    x = f32_to_bf16_bits(rng.standard_normal((24, 1024), dtype=np.float32))
+    w = f32_to_bf16_bits(rng.standard_normal((512, 1024), dtype=np.float32) * np.float32(0.02))
+    lo, hi = orc.chunk_bounds(1024, world)[rank]
+    to_dev = lambda b: torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16).cuda()
+    xd, wd = to_dev(x[:, lo:hi]), to_dev(w[:, lo:hi])
+    y = torch.empty(24, 512, dtype=torch.bfloat16, device="cuda")
+    c.rowparallel_gemm_ar(xd.data_ptr(), wd.data_ptr(), y.data_ptr(), 24, hi - lo, 512, stream_obj=stream)
+    assert c.read_status(stream) == 0
+    ref = orc.rowparallel_reference(bf16_bits_to_f32(x), bf16_bits_to_f32(w))
+    np.testing.assert_allclose(y.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+    torch.cuda.synchronize()
+    dist.barrier()
+    del c
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_core_communicator_two_gpus(torch_cuda, kinetic_rt):
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_core_comm_worker, args=(2, port), nprocs=2, join=True)
