@@ -460,6 +460,37 @@ namespace {
 int run_projection(PagedParams& p, const void* weight, int weight_rows, const char* name, cudaStream_t s) {
   const int tiles = (weight_rows + 127) / 128;
   const int num_kb = p.d_model / kBK;
+  // Many tiles (split-K would not split): the persistent kernel, one CTA per
+  // SM walking the tiles with the weight stream never drained.
+  // KRT_PROJ_PERSISTENT=0 / 1 forces either kernel.
+  const int forced = env_int("KRT_PROJ_PERSISTENT", -1);
+  if (forced == 1 || (forced != 0 && 2 * tiles > device_sm_count())) {
+    const size_t budget = smem_cap_bytes() - proj_persistent_smem_bytes(0, 1, p.n_pad);
+    int kc = 2;
+    if (num_kb % 2 != 0 || budget / (2 * (16384 + (size_t)p.n_pad * 128)) < 3) kc = 1;
+    int stages = (int)(budget / ((size_t)kc * (16384 + (size_t)p.n_pad * 128)));
+    if (stages > 8) stages = 8;
+    if (stages >= 2) {
+      p.kc = kc;
+      p.stages = stages;
+      p.splits = 1;
+      int cols = 32;
+      while (cols < 2 * p.n_pad) cols <<= 1;
+      p.tmem_cols = cols;
+      CUtensorMap tmap_w, tmap_x;
+      int rc = make_tmap_bf16_3d(&tmap_w, weight, (uint64_t)weight_rows, (uint64_t)p.d_model, (uint64_t)p.d_model,
+                                 128, (uint32_t)kc);
+      if (rc) return rc;
+      rc = make_tmap_bf16_3d(&tmap_x, p.xhat, (uint64_t)p.num_tokens, (uint64_t)p.d_model, (uint64_t)p.d_model,
+                             (uint32_t)p.n_pad, (uint32_t)kc);
+      if (rc) return rc;
+      cudaError_t e = launch_qkv_prep(p, s);
+      if (e != cudaSuccess) return cuda_error(e, name);
+      e = launch_proj_persistent(tmap_w, tmap_x, p, tiles, s);
+      if (e != cudaSuccess) return cuda_error(e, name);
+      return clear_error();
+    }
+  }
   const DecodeCfg cfg = decode_config(tiles, num_kb, p.n_pad, true);
   p.kc = cfg.kc;
   p.stages = cfg.stages;

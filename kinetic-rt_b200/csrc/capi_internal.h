@@ -50,6 +50,11 @@ size_t prefill_smem_bytes();
 cudaError_t launch_qkv_rope_prefill(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                     int tiles_per_block, cudaStream_t stream);
 
+// proj_persistent.cu
+size_t proj_persistent_smem_bytes(int stages, int kc, int n_pad);
+cudaError_t launch_proj_persistent(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
+                                   int num_tiles, cudaStream_t stream);
+
 // gemm_ar.cu
 struct GemmArParams;
 size_t gemm_ar_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits);

@@ -33,11 +33,16 @@ def dev(torch, a):
     return torch.from_numpy(f32_to_bf16_bits(a).view(np.int16)).view(torch.bfloat16).cuda()
 
 
-def test_gate_up_swiglu(torch_cuda):
+@pytest.mark.parametrize("persistent,T,I", [("0", 37, 320), ("1", 37, 320), ("auto", 128, 9600), ("1", 200, 704)])
+def test_gate_up_swiglu(torch_cuda, monkeypatch, persistent, T, I):
+    """Split-K kernel (few tiles) and the persistent kernel (many tiles: 150
+    tiles on 148 SMs gives two tiles to some CTAs, through both TMEM buffers)."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
+    if persistent != "auto":
+        monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
     rng = np.random.Generator(np.random.PCG64(1))
-    T, D, I = 37, 512, 320
+    D = 512
     x, g = bf(rng, T, D), bf(rng, D, scale=0.1, base=1.0)
     wg, wu = bf(rng, I, D, scale=0.05), bf(rng, I, D, scale=0.05)
     act = torch.full((T, I + 16), 5.0, dtype=torch.bfloat16, device="cuda")[:, :I]
@@ -58,13 +63,17 @@ def _check_argmax(logits, idx):
     return np.mean(idx == logits.argmax(-1))
 
 
-def test_lm_head_argmax_two_shards(torch_cuda):
-    """Two vocabulary shards (1000 + 777 rows, neither a multiple of 128) folded
-    into one key array give the argmax over the whole vocabulary."""
+@pytest.mark.parametrize("persistent,V0,V1", [("0", 1000, 777), ("1", 1000, 777), ("auto", 40000, 1777)])
+def test_lm_head_argmax_two_shards(torch_cuda, monkeypatch, persistent, V0, V1):
+    """Two vocabulary shards (neither a multiple of 128 rows) folded into one
+    key array give the argmax over the whole vocabulary; split-K and
+    persistent kernels (313 tiles: three tiles for some CTAs)."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
+    if persistent != "auto":
+        monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
     rng = np.random.Generator(np.random.PCG64(2))
-    T, D, V0, V1 = 19, 256, 1000, 777
+    T, D = 19, 256
     x, g = bf(rng, T, D), bf(rng, D, scale=0.1, base=1.0)
     w = bf(rng, V0 + V1, D, scale=0.05)
     keys = torch.zeros(T, dtype=torch.int64, device="cuda")
@@ -218,8 +227,11 @@ def test_decode_steps_tensor_parallel_match_oracle(torch_cuda):
     mp.spawn(_tp_decoder_worker, args=(2, port), nprocs=2, join=True)
 
 
-def test_decode_steps_match_oracle(torch_cuda):
+@pytest.mark.parametrize("persistent", ["0", "1"])
+def test_decode_steps_match_oracle(torch_cuda, monkeypatch, persistent):
     """Three graph-replayed decode steps of a 2-layer model, 5 sequences at
     ragged positions, against the oracle step by step (the oracle's token is
-    fed back on both sides, so a near-tie cannot make the runs diverge)."""
+    fed back on both sides, so a near-tie cannot make the runs diverge);
+    gate/up and lm_head on either projection kernel."""
+    monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
     run_decoder_against_oracle(torch_cuda)
