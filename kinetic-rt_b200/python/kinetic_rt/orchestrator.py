@@ -1,9 +1,11 @@
 """Host-side helpers around the hot path (python/kinetic_rt/orchestrator.py of
 the reference, reduced to what callers of the hot path use): the zero-copy and
 device-residency checks applied before pointers cross into native code, the
-stream context, and a runtime that loads .kin artifacts and checks their TP
-degree.  The reference's token-generation loop re-runs a full model that it
-does not have; that loop is outside this build (generate() says so).
+stream context, and a runtime that loads .kin artifacts, checks their TP
+degree and generates tokens through an attached paged decoder
+(decoder.PagedDecoder): the reference's loop (orchestrator.py:419-448)
+re-runs the whole model per token; here every token is one graph-replayed
+decode step that reuses the cached K/V.
 """
 import glob
 import os
@@ -105,6 +107,7 @@ class KineticRuntime:
         self.serializer = Serializer()
         self.max_seq_len = int(max_seq_len)
         self.model_path = None
+        self.decoder, self.tokenizer, self._graph = None, None, None
 
     def load_model(self, model_dir, tensor_parallel_degree=1):
         kins = sorted(glob.glob(os.path.join(model_dir, "*.kin")))
@@ -117,5 +120,51 @@ class KineticRuntime:
         self.model_path = kins[0]
         return kins[0]
 
-    def generate(self, prompt, max_tokens=16):
-        raise NotImplementedError("token generation over a full decoder stack is outside this build's hot path")
+    def attach_decoder(self, decoder, tokenizer=None):
+        """A decoder.PagedDecoder (batch 1) that generate() drives; `tokenizer`
+        is any object with encode(str) -> ids and decode(ids) -> str."""
+        if decoder.B != 1:
+            raise RuntimeConfigurationError("generate() drives a decoder of batch 1")
+        self.decoder, self.tokenizer = decoder, tokenizer
+        self._graph = None
+
+    def encode_prompt(self, prompt):
+        """Token ids of the prompt: the tokenizer's, else its UTF-8 bytes (the
+        reference's fallback, orchestrator.py:303-313)."""
+        ids = self.tokenizer.encode(prompt) if getattr(self, "tokenizer", None) else list(prompt.encode("utf-8"))
+        return [int(t) for t in ids]
+
+    def generate_ids(self, prompt_ids, max_new_tokens=10):
+        """Greedy continuation of `prompt_ids` (a list of ints): the prompt is
+        fed one token per decode step (its K/V cached as it goes), then each
+        step's argmax (orchestrator.py:442-444) becomes the next input.
+        Returns the new token ids."""
+        dec = getattr(self, "decoder", None)
+        if dec is None:
+            raise RuntimeConfigurationError("no decoder attached (KineticRuntime.attach_decoder)")
+        if not prompt_ids:
+            raise RuntimeConfigurationError("empty prompt")
+        if len(prompt_ids) + max_new_tokens > dec.max_seq_len:
+            raise ContextWindowExceededError("prompt and new tokens exceed the decoder's max_seq_len")
+        torch = dec.torch
+        dec.start([prompt_ids[0]], [0])
+        if self._graph is None:
+            self._graph = dec.capture()
+        feed = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        out = []
+        for i in range(len(prompt_ids) - 1 + max_new_tokens):
+            feed[0] = prompt_ids[i + 1] if i + 1 < len(prompt_ids) else -1
+            dec.next_input.copy_(feed, non_blocking=True)
+            self._graph.replay()
+            if i + 1 >= len(prompt_ids):
+                out.append(int(dec.tokens[0].item()))
+        dec.check_status()
+        return out
+
+    def generate(self, prompt, max_new_tokens=10):
+        """Text in, text out (the reference's generate, orchestrator.py:419-448)."""
+        ids = self.encode_prompt(prompt)
+        ids = ids + self.generate_ids(ids, max_new_tokens)
+        if getattr(self, "tokenizer", None):
+            return self.tokenizer.decode(ids)
+        return bytes(t % 256 for t in ids).decode("utf-8", errors="replace")

@@ -235,3 +235,38 @@ def test_decode_steps_match_oracle(torch_cuda, monkeypatch, persistent):
     gate/up and lm_head on either projection kernel."""
     monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
     run_decoder_against_oracle(torch_cuda)
+
+
+def test_runtime_generate_matches_oracle(torch_cuda):
+    """KineticRuntime.generate_ids over an attached batch-1 decoder: the
+    prompt is fed token by token, then greedy tokens; equal to the oracle's
+    greedy continuation (steps whose top-two logits are a near-tie excepted)."""
+    torch = torch_cuda
+    from python.kinetic_rt.decoder import PagedDecoder, RankWeights
+    from python.kinetic_rt.orchestrator import KineticRuntime
+    rng = np.random.Generator(np.random.PCG64(9))
+    shape, full = tiny_model(rng)
+    dec = PagedDecoder(torch, shape, RankWeights.from_full(torch, shape, full, 0, 1), 1, 48)
+    rt = KineticRuntime.__new__(KineticRuntime)
+    rt.decoder = rt.tokenizer = rt._graph = None
+    rt.attach_decoder(dec)
+    prompt = [int(t) for t in rng.integers(0, shape.vocab, size=6)]
+    got = rt.generate_ids(prompt, max_new_tokens=5)
+    # oracle: the same steps on the CPU
+    table = dec.block_table.cpu().numpy()
+    pools = [np.zeros((dec.num_blocks, 16, 2, shape.n_kv_heads, 128), np.float32) for _ in range(shape.n_layers)]
+    cos, sin = fused_layer.rope_tables(np.arange(48), 128, shape.rope_theta)
+    h = full["embed"][[prompt[0]]]
+    seq, ref, ties = list(prompt), [], []
+    for pos in range(len(prompt) - 1 + 5):
+        logits, tok, _ = odec.decode_step(full, h, np.array([pos]), table, pools, cos, sin, shape.n_heads,
+                                          shape.n_kv_heads, 16)
+        top2 = np.sort(logits[0])[-2:]
+        if pos + 1 >= len(prompt):
+            ref.append(int(tok[0]))
+            ties.append(top2[1] - top2[0] < ATOL + RTOL * abs(top2[1]))
+            nxt = got[len(ref) - 1]  # follow the GPU's choice so a near-tie cannot derail the comparison
+        else:
+            nxt = prompt[pos + 1]
+        h = full["embed"][[nxt]]
+    assert all(g == r or t for g, r, t in zip(got, ref, ties)), (got, ref, ties)
