@@ -150,11 +150,13 @@ class KineticRuntime:
         dec.start([prompt_ids[0]], [0])
         if self._graph is None:
             self._graph = dec.capture()
-        feed = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        steps = len(prompt_ids) - 1 + max_new_tokens
+        # one pinned slot per step: a slot is not rewritten while its copy may still be queued
+        feed = torch.tensor([prompt_ids[i + 1] if i + 1 < len(prompt_ids) else -1 for i in range(steps)],
+                            dtype=torch.int32).pin_memory()
         out = []
-        for i in range(len(prompt_ids) - 1 + max_new_tokens):
-            feed[0] = prompt_ids[i + 1] if i + 1 < len(prompt_ids) else -1
-            dec.next_input.copy_(feed, non_blocking=True)
+        for i in range(steps):
+            dec.next_input.copy_(feed[i:i + 1], non_blocking=True)
             self._graph.replay()
             if i + 1 >= len(prompt_ids):
                 out.append(int(dec.tokens[0].item()))
