@@ -466,7 +466,7 @@ int run_projection(PagedParams& p, const void* weight, int weight_rows, const ch
   const int forced = env_int("KRT_PROJ_PERSISTENT", -1);
   if (forced == 1 || (forced != 0 && 2 * tiles > device_sm_count())) {
     const size_t budget = smem_cap_bytes() - proj_persistent_smem_bytes(0, 1, p.n_pad);
-    int kc = 2;
+    int kc = env_int("KRT_PROJ_KC", 2) == 1 ? 1 : 2;
     if (num_kb % 2 != 0 || budget / (2 * (16384 + (size_t)p.n_pad * 128)) < 3) kc = 1;
     int stages = (int)(budget / ((size_t)kc * (16384 + (size_t)p.n_pad * 128)));
     if (stages > 8) stages = 8;
