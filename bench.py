@@ -1112,6 +1112,88 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
+def run_kernel(args, rank, world, local_rank):
+    """--workload kernel --kernel NAME: one kernel of the decode step alone, at
+    the stack's shapes (batch 128, context 4224, this TP degree's shards), run
+    --steps times back to back; a short case for ncu captures (a few GB on the
+    device).  Prints one JSON line with the mean time per call."""
+    import torch
+    from python.kinetic_rt import _lib
+    from python.kinetic_rt.decoder import rope_cache
+    torch.cuda.set_device(local_rank)
+    tp = args.tp or world
+    B, ctx, D = STACK_BATCH, PROMPT + GEN_STEPS // 2, HIDDEN
+    H, KV, I, V = N_HEADS // tp, N_KV // tp, INTER // tp, -(-VOCAB // tp)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(B, D, generator=g, device="cuda").to(torch.bfloat16)
+    gam = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+    name = args.kernel
+    if name == "paged_attention":
+        bps = -(-ctx // BLOCK) + 1
+        nb = B * bps
+        pool = torch.randn(nb, BLOCK, 2 * KV * HEAD_DIM, generator=g, device="cuda").to(torch.bfloat16)
+        table = torch.randperm(nb, device="cuda").to(torch.int32).view(B, bps)
+        lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+        q = torch.randn(B, H * HEAD_DIM, generator=g, device="cuda").to(torch.bfloat16)
+        o = torch.empty_like(q)
+        ws = torch.zeros(_lib.attention_workspace_bytes(B, H, KV, ctx), dtype=torch.uint8, device="cuda")
+        a = _lib.attention_args(q, pool, table, lens, o, H, KV, nb, BLOCK, ctx, ws)
+        run = lambda: _lib.paged_attention_decode(a)
+    elif name == "gate_up_swiglu":
+        w = (torch.randn(2 * I, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        act = torch.empty(B, I, device="cuda", dtype=torch.bfloat16)
+        ws = torch.zeros(_lib.projection_workspace_bytes(B, D), dtype=torch.uint8, device="cuda")
+        a = _lib.gate_up_args(x, gam, w, act, ws)
+        run = lambda: _lib.gate_up_swiglu(a)
+    elif name == "lm_head_argmax":
+        w = (torch.randn(V, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        keys = torch.zeros(B, dtype=torch.int64, device="cuda")
+        ws = torch.zeros(_lib.projection_workspace_bytes(B, D), dtype=torch.uint8, device="cuda")
+        a = _lib.lm_head_args(x, gam, w, keys, ws)
+        run = lambda: _lib.lm_head_argmax(a)
+    elif name in ("o_proj_gemm_ar", "down_proj_gemm_ar"):
+        K = H * HEAD_DIM if name == "o_proj_gemm_ar" else I
+        w = (torch.randn(D, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        xx = torch.randn(B, K, generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.zeros(B, D, device="cuda", dtype=torch.bfloat16)
+        ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+        a = _lib.gemm_ar_args(xx, w, y, ws, residual=y)
+        run = lambda: _lib.rowparallel_gemm_ar(None, a)
+    elif name == "qkv_rope_decode":
+        rows = (H + 2 * KV) * HEAD_DIM
+        w = (torch.randn(rows, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        cos, sin = rope_cache(torch, ctx + 1, HEAD_DIM, 5e5)
+        pos = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+        seq = torch.arange(B, dtype=torch.int32, device="cuda")
+        bps = -(-(ctx + 1) // BLOCK)
+        bt = torch.arange(B * bps, dtype=torch.int32, device="cuda").view(B, bps)
+        pool = torch.zeros(B * bps, BLOCK, 2 * KV * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+        qq = torch.empty(B, H * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+        ws = torch.zeros(_lib.decode_workspace_bytes(B, D, H, KV), dtype=torch.uint8, device="cuda")
+        a = _lib.paged_args(x, w, None, gam, cos, sin, pos, seq, bt, pool, qq, H, KV, B * bps, BLOCK, ws)
+        run = lambda: _lib.qkv_rope_decode(a)
+    else:
+        raise SystemExit(f"unknown kernel {name}")
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    rc, bits = _lib.read_status(ws)
+    if rc != 0:
+        raise RuntimeError(f"{name} status {bits:#x}")
+    nbytes = stack_kernel_bytes(tp, ctx)[name][0]
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    if rank == 0:
+        print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "calls": args.steps, "us": round(us, 2),
+                          "algorithmic_bytes": nbytes, "GBps": round(nbytes / us / 1e3, 1),
+                          "note": "back-to-back eager calls (launch gaps included); a profiling case"}), flush=True)
+
+
 def run_reference_stack(args, world):
     """The stack's metric on the CPU path: each of min(K, 3) samples is one
     bounded sample (cpu_stack_sample) of a decode step; value = tokens/s."""
@@ -1138,14 +1220,18 @@ def main():
                     help="timed steps (default: 64 decode steps of the stack, 20000 layer steps)")
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["krt", "reference"], default="krt")
-    ap.add_argument("--workload", choices=["stack", "layer", "prefill", "gemm_ar"], default="stack",
+    ap.add_argument("--kernel", default="paged_attention",
+                    help="--workload kernel: paged_attention, qkv_rope_decode, o_proj_gemm_ar, gate_up_swiglu, "
+                         "down_proj_gemm_ar, lm_head_argmax")
+    ap.add_argument("--tp", type=int, default=0, help="--workload kernel: TP degree whose shard shapes to use")
+    ap.add_argument("--workload", choices=["stack", "layer", "prefill", "gemm_ar", "kernel"], default="stack",
                     help="stack: decode steps of the Llama-3-8B-shaped stack (default); layer: one decoder layer's "
                          "hot path; prefill: the fused QKV prefill kernel alone")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 64 if args.workload == "stack" else 20000
+        args.steps = {"stack": 64, "kernel": 4}.get(args.workload, 20000)
     if args.warmup is None:
-        args.warmup = 8 if args.workload == "stack" else 50
+        args.warmup = {"stack": 8, "kernel": 1}.get(args.workload, 50)
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
@@ -1161,6 +1247,8 @@ def main():
         run_krt(args, rank, world, local_rank)
     elif args.workload == "gemm_ar":
         run_gemm_ar(args, rank, world, local_rank)
+    elif args.workload == "kernel":
+        run_kernel(args, rank, world, local_rank)
     else:
         run_stack(args, rank, world, local_rank)
 
