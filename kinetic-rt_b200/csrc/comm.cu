@@ -471,6 +471,10 @@ int gemm_stages(int tile_m, int n_pad, int kc, int splits) {
 // Box depth with the most weight bytes in flight, leaving every split at
 // least one box of the K range.
 int gemm_kc(int tile_m, int num_kb, int n_pad, int splits) {
+  const int forced = env_int_value("KRT_GEMM_KC", 0);  // box depth for tuning
+  if ((forced == 1 || forced == 2 || forced == 4) && num_kb % forced == 0 && num_kb / forced >= splits &&
+      gemm_stages(tile_m, n_pad, forced, splits) >= 1)
+    return forced;
   int best = 1;
   size_t best_bytes = 0;
   for (int kc = 4; kc >= 1; kc >>= 1) {
