@@ -1114,9 +1114,11 @@ def run_reference(args, rank, world):
 
 def run_kernel(args, rank, world, local_rank):
     """--workload kernel --kernel NAME: one kernel of the decode step alone, at
-    the stack's shapes (batch 128, context 4224, this TP degree's shards), run
-    --steps times back to back; a short case for ncu captures (a few GB on the
-    device).  Prints one JSON line with the mean time per call."""
+    the stack's shapes (batch 128, context 4224, the shards of TP = --tp),
+    cycling through enough weight copies that they exceed L2 twice over,
+    --steps calls per CUDA graph, the graph replayed after --warmup eager
+    calls.  A short case for knob sweeps and ncu captures (a few GB on the
+    device).  Prints one JSON line with the device time per call."""
     import torch
     from python.kinetic_rt import _lib
     from python.kinetic_rt.decoder import rope_cache
@@ -1128,6 +1130,8 @@ def run_kernel(args, rank, world, local_rank):
     x = torch.randn(B, D, generator=g, device="cuda").to(torch.bfloat16)
     gam = torch.ones(D, device="cuda", dtype=torch.bfloat16)
     name = args.kernel
+    copies = lambda nbytes: max(1, -(-2 * L2_BYTES // nbytes))
+    rnd = lambda *sz: (torch.randn(*sz, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
     if name == "paged_attention":
         bps = -(-ctx // BLOCK) + 1
         nb = B * bps
@@ -1137,31 +1141,27 @@ def run_kernel(args, rank, world, local_rank):
         q = torch.randn(B, H * HEAD_DIM, generator=g, device="cuda").to(torch.bfloat16)
         o = torch.empty_like(q)
         ws = torch.zeros(_lib.attention_workspace_bytes(B, H, KV, ctx), dtype=torch.uint8, device="cuda")
-        a = _lib.attention_args(q, pool, table, lens, o, H, KV, nb, BLOCK, ctx, ws)
-        run = lambda: _lib.paged_attention_decode(a)
+        args_list = [_lib.attention_args(q, pool, table, lens, o, H, KV, nb, BLOCK, ctx, ws)]
+        call = _lib.paged_attention_decode
     elif name == "gate_up_swiglu":
-        w = (torch.randn(2 * I, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
         act = torch.empty(B, I, device="cuda", dtype=torch.bfloat16)
         ws = torch.zeros(_lib.projection_workspace_bytes(B, D), dtype=torch.uint8, device="cuda")
-        a = _lib.gate_up_args(x, gam, w, act, ws)
-        run = lambda: _lib.gate_up_swiglu(a)
+        args_list = [_lib.gate_up_args(x, gam, rnd(2 * I, D), act, ws) for _ in range(copies(2 * I * D * 2))]
+        call = _lib.gate_up_swiglu
     elif name == "lm_head_argmax":
-        w = (torch.randn(V, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
         keys = torch.zeros(B, dtype=torch.int64, device="cuda")
         ws = torch.zeros(_lib.projection_workspace_bytes(B, D), dtype=torch.uint8, device="cuda")
-        a = _lib.lm_head_args(x, gam, w, keys, ws)
-        run = lambda: _lib.lm_head_argmax(a)
+        args_list = [_lib.lm_head_args(x, gam, rnd(V, D), keys, ws) for _ in range(copies(V * D * 2))]
+        call = _lib.lm_head_argmax
     elif name in ("o_proj_gemm_ar", "down_proj_gemm_ar"):
         K = H * HEAD_DIM if name == "o_proj_gemm_ar" else I
-        w = (torch.randn(D, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
         xx = torch.randn(B, K, generator=g, device="cuda").to(torch.bfloat16)
         y = torch.zeros(B, D, device="cuda", dtype=torch.bfloat16)
         ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
-        a = _lib.gemm_ar_args(xx, w, y, ws, residual=y)
-        run = lambda: _lib.rowparallel_gemm_ar(None, a)
+        args_list = [_lib.gemm_ar_args(xx, rnd(D, K), y, ws, residual=y) for _ in range(copies(D * K * 2))]
+        call = lambda a: _lib.rowparallel_gemm_ar(None, a)
     elif name == "qkv_rope_decode":
         rows = (H + 2 * KV) * HEAD_DIM
-        w = (torch.randn(rows, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
         cos, sin = rope_cache(torch, ctx + 1, HEAD_DIM, 5e5)
         pos = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
         seq = torch.arange(B, dtype=torch.int32, device="cuda")
@@ -1170,28 +1170,38 @@ def run_kernel(args, rank, world, local_rank):
         pool = torch.zeros(B * bps, BLOCK, 2 * KV * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
         qq = torch.empty(B, H * HEAD_DIM, dtype=torch.bfloat16, device="cuda")
         ws = torch.zeros(_lib.decode_workspace_bytes(B, D, H, KV), dtype=torch.uint8, device="cuda")
-        a = _lib.paged_args(x, w, None, gam, cos, sin, pos, seq, bt, pool, qq, H, KV, B * bps, BLOCK, ws)
-        run = lambda: _lib.qkv_rope_decode(a)
+        args_list = [_lib.paged_args(x, rnd(rows, D), None, gam, cos, sin, pos, seq, bt, pool, qq, H, KV, B * bps,
+                                     BLOCK, ws) for _ in range(copies(rows * D * 2))]
+        call = _lib.qkv_rope_decode
     else:
         raise SystemExit(f"unknown kernel {name}")
-    for _ in range(args.warmup):
-        run()
+    n = len(args_list)
+    for i in range(args.warmup):
+        call(args_list[i % n])
     torch.cuda.synchronize()
+    calls = max(args.steps, n)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(calls):
+            call(args_list[i % n])
+    graph.replay()
+    torch.cuda.synchronize()
+    reps = 3
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        run()
+    for _ in range(reps):
+        graph.replay()
     e1.record()
     torch.cuda.synchronize()
     rc, bits = _lib.read_status(ws)
     if rc != 0:
         raise RuntimeError(f"{name} status {bits:#x}")
     nbytes = stack_kernel_bytes(tp, ctx)[name][0]
-    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
     if rank == 0:
-        print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "calls": args.steps, "us": round(us, 2),
-                          "algorithmic_bytes": nbytes, "GBps": round(nbytes / us / 1e3, 1),
-                          "note": "back-to-back eager calls (launch gaps included); a profiling case"}), flush=True)
+        print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "calls_per_graph": calls,
+                          "weight_copies": n, "us": round(us, 2), "algorithmic_bytes": nbytes,
+                          "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
 
 
 def run_reference_stack(args, world):
