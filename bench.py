@@ -723,10 +723,10 @@ def run_gemm_ar(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def stack_kernel_bytes(world, ctx):
+def stack_kernel_bytes(world, ctx, batch=STACK_BATCH):
     """Algorithmic bytes per launch of each kernel of the decode step (this
     rank's share): every input read once, every output written once."""
-    B, D = STACK_BATCH, HIDDEN
+    B, D = batch, HIDDEN
     hq, hkv, ir = N_HEADS // world, N_KV // world, INTER // world
     vr = -(-VOCAB // world)
     qkv_rows = (hq + 2 * hkv) * HEAD_DIM
@@ -1124,7 +1124,7 @@ def run_kernel(args, rank, world, local_rank):
     from python.kinetic_rt.decoder import rope_cache
     torch.cuda.set_device(local_rank)
     tp = args.tp or world
-    B, ctx, D = STACK_BATCH, PROMPT + GEN_STEPS // 2, HIDDEN
+    B, ctx, D = args.batch or STACK_BATCH, PROMPT + GEN_STEPS // 2, HIDDEN
     H, KV, I, V = N_HEADS // tp, N_KV // tp, INTER // tp, -(-VOCAB // tp)
     g = torch.Generator(device="cuda").manual_seed(0)
     x = torch.randn(B, D, generator=g, device="cuda").to(torch.bfloat16)
@@ -1196,10 +1196,10 @@ def run_kernel(args, rank, world, local_rank):
     rc, bits = _lib.read_status(ws)
     if rc != 0:
         raise RuntimeError(f"{name} status {bits:#x}")
-    nbytes = stack_kernel_bytes(tp, ctx)[name][0]
+    nbytes = stack_kernel_bytes(tp, ctx, B)[name][0]
     us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
     if rank == 0:
-        print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "calls_per_graph": calls,
+        print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "batch": B, "calls_per_graph": calls,
                           "weight_copies": n, "us": round(us, 2), "algorithmic_bytes": nbytes,
                           "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
 
@@ -1234,6 +1234,7 @@ def main():
                     help="--workload kernel: paged_attention, qkv_rope_decode, o_proj_gemm_ar, gate_up_swiglu, "
                          "down_proj_gemm_ar, lm_head_argmax")
     ap.add_argument("--tp", type=int, default=0, help="--workload kernel: TP degree whose shard shapes to use")
+    ap.add_argument("--batch", type=int, default=0, help="--workload kernel: tokens per call (default 128)")
     ap.add_argument("--workload", choices=["stack", "layer", "prefill", "gemm_ar", "kernel"], default="stack",
                     help="stack: decode steps of the Llama-3-8B-shaped stack (default); layer: one decoder layer's "
                          "hot path; prefill: the fused QKV prefill kernel alone")
