@@ -474,6 +474,7 @@ int run_projection(PagedParams& p, const void* weight, int weight_rows, const ch
       p.kc = kc;
       p.stages = stages;
       p.splits = 1;
+      p.prefetch = env_int("KRT_L2_PREFETCH_STAGES", 0);
       int cols = 32;
       while (cols < 2 * p.n_pad) cols <<= 1;
       p.tmem_cols = cols;

@@ -104,6 +104,9 @@ __global__ void __launch_bounds__(kPjThreads, 1)
       tma_load_3d(a_smem + (size_t)it * a_stage, &tmap_w, &tl->full[it], 0, tile_of(it) * 128, (it % num_kc) * KC,
                   pol_w);
     }
+    // optionally the next p.prefetch stages' weights into L2 beyond the ring
+    for (int it = pre; it < total && it < pre + p.prefetch; ++it)
+      tma_prefetch_l2_3d(&tmap_w, 0, tile_of(it) * 128, (it % num_kc) * KC);
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
@@ -137,6 +140,8 @@ __global__ void __launch_bounds__(kPjThreads, 1)
         tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, tile_of(it) * 128, (it % num_kc) * KC,
                     pol_w);
         tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (it % num_kc) * KC, pol_x);
+        const int pf = it + p.prefetch;
+        if (p.prefetch > 0 && pf < total) tma_prefetch_l2_3d(&tmap_w, 0, tile_of(pf) * 128, (pf % num_kc) * KC);
       }
     }
   } else if (warp == 1) {
