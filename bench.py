@@ -1131,7 +1131,12 @@ def run_kernel(args, rank, world, local_rank):
     gam = torch.ones(D, device="cuda", dtype=torch.bfloat16)
     name = args.kernel
     copies = lambda nbytes: max(1, -(-2 * L2_BYTES // nbytes))
-    rnd = lambda *sz: (torch.randn(*sz, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    keep = []  # every tensor an argument struct points to stays referenced (the structs hold raw pointers)
+
+    def rnd(*sz):
+        t = (torch.randn(*sz, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        keep.append(t)
+        return t
     if name == "paged_attention":
         bps = -(-ctx // BLOCK) + 1
         nb = B * bps
@@ -1198,6 +1203,7 @@ def run_kernel(args, rank, world, local_rank):
         raise RuntimeError(f"{name} status {bits:#x}")
     nbytes = stack_kernel_bytes(tp, ctx, B)[name][0]
     us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+    del graph, keep
     if rank == 0:
         print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "batch": B, "calls_per_graph": calls,
                           "weight_copies": n, "us": round(us, 2), "algorithmic_bytes": nbytes,

@@ -301,7 +301,9 @@ KRT_API int krt_rowparallel_gemm_ar(krt_comm* comm, const krt_gemm_ar_args* args
  * + p % tokens_per_block (token layout [K | V][kv_head][128] bf16).  fp32
  * accumulation and softmax; head_dim 128; at most 16 query heads per KV head;
  * tokens_per_block a multiple of 16.  A sequence with seq_lens <= 0 gets
- * zeros.  Out-of-range block ids are masked and set status bit 8.  The
+ * zeros; one with seq_lens > max_seq_len attends over its first max_seq_len
+ * tokens and sets status bit 8.  Out-of-range block ids are masked and set
+ * status bit 8.  The
  * workspace (krt_paged_attention_workspace_size bytes) is zero-filled once
  * when allocated; the kernel leaves its counters at zero after every call.
  * ---------------------------------------------------------------------- */

@@ -62,6 +62,7 @@ struct AttnParams {
   int n_heads, n_kv_heads, group;
   int q_stride, out_stride;
   int chunks_per_split, max_splits;
+  int max_len;               // the grid covers this many tokens per sequence
   float scale_log2;          // softmax scale * log2(e)
 };
 
@@ -121,7 +122,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   pdl_wait();  // q and the pool come from the previous kernel
   pdl_launch_dependents();
 
-  const int len = p.seq_lens[b];
+  int len = p.seq_lens[b];
+  if (len > p.max_len) {
+    // beyond the grid (and the workspace): attend over the first max_len tokens and report it
+    if (threadIdx.x == 0 && z == 0) atomicOr(p.status, kStatusBadBlock);
+    len = p.max_len;
+  }
   const int n_chunks = len > 0 ? (len + kAttnChunk - 1) / kAttnChunk : 0;
   const int splits = n_chunks > 0 ? (n_chunks + p.chunks_per_split - 1) / p.chunks_per_split : 1;
   if (z >= splits) return;  // the whole CTA: nothing of this sequence left for it
@@ -487,6 +493,7 @@ extern "C" int krt_paged_attention_decode(const krt_paged_attention_args* a, voi
   p.group = a->n_heads / a->n_kv_heads;
   p.q_stride = a->q_stride;
   p.out_stride = a->out_stride;
+  p.max_len = a->max_seq_len;
   p.chunks_per_split = attn_chunks_per_split(a->num_seqs, a->n_kv_heads, max_chunks);
   p.max_splits = (max_chunks + p.chunks_per_split - 1) / p.chunks_per_split;
   const float scale = a->scale > 0.f ? a->scale : 0.08838834764831845f;  // 1 / sqrt(128)

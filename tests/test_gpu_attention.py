@@ -99,3 +99,31 @@ def test_attention_bad_block_sets_status(torch_cuda):
     rc, bits = _lib.read_status(ws)
     assert bits & 8
     assert torch.isfinite(out.float()).all()
+
+
+def test_attention_length_beyond_max_is_clamped(torch_cuda):
+    """A sequence longer than max_seq_len attends over its first max_seq_len
+    tokens and reports status bit 8; the split counters stay consistent, so
+    the next call is exact."""
+    torch = torch_cuda
+    from python.kinetic_rt import _lib
+    rng = np.random.Generator(np.random.PCG64(21))
+    S, H, KV, max_len = 3, 8, 2, 300
+    bps = -(-max_len // 16) + 2
+    nb = S * bps
+    table = rng.permutation(nb).astype(np.int32).reshape(S, bps)
+    pool = f32_to_bf16_bits(rng.standard_normal((nb, 16, 2, KV, 128), dtype=np.float32))
+    qb = f32_to_bf16_bits(rng.standard_normal((S, H, 128), dtype=np.float32))
+    q, pool_d = to_dev(torch, qb.reshape(S, -1)), to_dev(torch, pool)
+    out = torch.empty(S, H * 128, dtype=torch.bfloat16, device="cuda")
+    ws = torch.zeros(_lib.attention_workspace_bytes(S, H, KV, max_len), dtype=torch.uint8, device="cuda")
+    table_d = torch.from_numpy(table).cuda()
+    for lens, bad in (([100, max_len + 25, 7], True), ([100, 250, 7], False)):
+        lens_d = torch.tensor(lens, dtype=torch.int32, device="cuda")  # referenced while the kernel runs
+        a = _lib.attention_args(q, pool_d, table_d, lens_d, out, H, KV, nb, 16, max_len, ws)
+        _lib.paged_attention_decode(a)
+        rc, bits = _lib.read_status(ws)
+        assert bool(bits & 8) == bad
+        ref = orc.paged_decode_attention(bf16_bits_to_f32(qb), bf16_bits_to_f32(pool), table,
+                                         [min(n, max_len) for n in lens], H, KV, 16)
+        np.testing.assert_allclose(out.float().cpu().numpy().reshape(S, H, 128), ref, atol=2e-2, rtol=1e-2)

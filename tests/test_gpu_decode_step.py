@@ -48,7 +48,8 @@ def test_gate_up_swiglu(torch_cuda, monkeypatch, persistent, T, I):
     act = torch.full((T, I + 16), 5.0, dtype=torch.bfloat16, device="cuda")[:, :I]
     ws = torch.zeros(_lib.projection_workspace_bytes(T, D), dtype=torch.uint8, device="cuda")
     wgu = _lib.interleave_gate_up(dev(torch, wg), dev(torch, wu)).contiguous()
-    _lib.gate_up_swiglu(_lib.gate_up_args(dev(torch, x), dev(torch, g), wgu, act, ws))
+    xd, gd = dev(torch, x), dev(torch, g)  # referenced while the kernels run (the structs hold raw pointers)
+    _lib.gate_up_swiglu(_lib.gate_up_args(xd, gd, wgu, act, ws))
     assert _lib.read_status(ws) == (0, 0)
     xm = round_bf16(fused_layer.rms_norm(x, g)).astype(np.float64)
     gg, uu = xm @ wg.astype(np.float64).T, xm @ wu.astype(np.float64).T
@@ -78,9 +79,9 @@ def test_lm_head_argmax_two_shards(torch_cuda, monkeypatch, persistent, V0, V1):
     w = bf(rng, V0 + V1, D, scale=0.05)
     keys = torch.zeros(T, dtype=torch.int64, device="cuda")
     ws = torch.zeros(_lib.projection_workspace_bytes(T, D), dtype=torch.uint8, device="cuda")
-    wd = dev(torch, w)
+    wd, xd, gd = dev(torch, w), dev(torch, x), dev(torch, g)
     for lo, hi in ((0, V0), (V0, V0 + V1)):
-        _lib.lm_head_argmax(_lib.lm_head_args(dev(torch, x), dev(torch, g), wd[lo:hi], keys, ws, vocab_offset=lo))
+        _lib.lm_head_argmax(_lib.lm_head_args(xd, gd, wd[lo:hi], keys, ws, vocab_offset=lo))
     assert _lib.read_status(ws) == (0, 0)
     k = keys.cpu().numpy().view(np.uint64)
     idx = (0xFFFFFFFF - (k & np.uint64(0xFFFFFFFF))).astype(np.int64)
@@ -123,9 +124,9 @@ def test_gemm_residual_in_place(torch_cuda):
     rng = np.random.Generator(np.random.PCG64(3))
     T, K, N = 21, 640, 384
     x, w, h = bf(rng, T, K), bf(rng, N, K, scale=0.02), bf(rng, T, N)
-    hd = dev(torch, h)
+    hd, xd, wdev = dev(torch, h), dev(torch, x), dev(torch, w)
     ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
-    _lib.rowparallel_gemm_ar(None, _lib.gemm_ar_args(dev(torch, x), dev(torch, w), hd, ws, residual=hd))
+    _lib.rowparallel_gemm_ar(None, _lib.gemm_ar_args(xd, wdev, hd, ws, residual=hd))
     assert _lib.read_status(ws) == (0, 0)
     ref = h.astype(np.float64) + x.astype(np.float64) @ w.astype(np.float64).T
     np.testing.assert_allclose(hd.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
