@@ -2,7 +2,9 @@
 
 This is the thinnest possible layer: struct mirrors, argument marshalling
 from torch tensors (data_ptr / strides / current stream) and error
-translation.  Loading fails loudly when the library is missing; there is no
+translation.  Every argument struct built here keeps references to the
+tensors whose raw pointers it holds (`_refs`), so a struct kept for later
+launches (or captured into a CUDA graph) cannot outlive its tensors.  Loading fails loudly when the library is missing; there is no
 fallback implementation.
 """
 import ctypes
@@ -236,6 +238,8 @@ def paged_args(x, qkv_weight, qkv_bias, rms_weight, rope_cos, rope_sin, position
     a.eps = float(eps)
     a.workspace = _ptr(workspace)
     a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    a._refs = (x, qkv_weight, qkv_bias, rms_weight, rope_cos, rope_sin, positions, token_seq, block_table, kv_pool,
+               q_out, k_out, v_out, workspace)
     return a
 
 
@@ -312,6 +316,7 @@ def gemm_ar_args(x, weight, y, workspace, residual=None):
     a.x_stride, a.y_stride = int(x.stride(0)), int(y.stride(0))
     a.workspace = _ptr(workspace)
     a.workspace_bytes = workspace.numel() * workspace.element_size()
+    a._refs = (x, weight, y, workspace, residual)
     return a
 
 
@@ -336,6 +341,7 @@ def attention_args(q, kv_pool, block_table, seq_lens, out, n_heads, n_kv_heads, 
     a.tokens_per_block, a.max_seq_len, a.scale = int(tokens_per_block), int(max_seq_len), float(scale)
     a.workspace = _ptr(workspace)
     a.workspace_bytes = workspace.numel() * workspace.element_size()
+    a._refs = (q, kv_pool, block_table, seq_lens, out, workspace)
     return a
 
 
@@ -359,6 +365,7 @@ def gate_up_args(x, rms_weight, gate_up_weight, act, workspace, eps=1e-5):
     a.eps = float(eps)
     a.workspace = _ptr(workspace)
     a.workspace_bytes = workspace.numel() * workspace.element_size()
+    a._refs = (x, rms_weight, gate_up_weight, act, workspace)
     return a
 
 
@@ -383,6 +390,7 @@ def lm_head_args(x, rms_weight, weight, keys, workspace, vocab_offset=0, eps=1e-
     a.eps = float(eps)
     a.workspace = _ptr(workspace)
     a.workspace_bytes = workspace.numel() * workspace.element_size()
+    a._refs = (x, rms_weight, weight, keys, workspace)
     return a
 
 
@@ -400,6 +408,7 @@ def greedy_step_args(keys, tokens, status, vocab, embedding=None, hidden=None, p
     a.d_model = 0 if embedding is None else int(embedding.shape[1])
     a.hidden_stride = 0 if hidden is None else int(hidden.stride(0))
     a.vocab = int(vocab)
+    a._refs = (keys, tokens, status, embedding, hidden, positions, seq_lens, next_input)
     return a
 
 

@@ -34,6 +34,7 @@ HOST_TESTS = ["test_graph.py", "test_aot.py", "test_validation.py", "test_distri
 
 
 def run(tests_dir, which, extra=()):
+    tests_dir = os.path.abspath(tests_dir)  # pytest runs from a scratch directory
     if os.path.isdir(os.path.join(tests_dir, "tests")):
         tests_dir = os.path.join(tests_dir, "tests")
     files = [os.path.join(tests_dir, f) for f in (GPU_TESTS if which == "gpu" else HOST_TESTS)]
