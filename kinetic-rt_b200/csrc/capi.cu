@@ -460,11 +460,26 @@ namespace {
 int run_projection(PagedParams& p, const void* weight, int weight_rows, const char* name, cudaStream_t s) {
   const int tiles = (weight_rows + 127) / 128;
   const int num_kb = p.d_model / kBK;
-  // Many tiles (split-K would not split): the persistent kernel, one CTA per
-  // SM walking the tiles with the weight stream never drained.
-  // KRT_PROJ_PERSISTENT=0 / 1 forces either kernel.
+  const int sms = device_sm_count();
+  // Kernel and work split by tiles per SM, as measured on B200 (148 SMs) at
+  // 128 tokens, gate/up + SwiGLU and lm_head + argmax at the Llama-3-8B TP
+  // shards (us per call):
+  //   gate/up TP=1 (224 tiles): stream-K 54.4, whole tiles 56.0, split-K 72.0
+  //   gate/up TP=2 (112):       stream-K 35.6, whole tiles 32.9, split-K 37.3
+  //   gate/up TP=4 (56):        stream-K 28.3, split-K 33.9
+  //   gate/up TP=8 (28):        stream-K 27.3, split-K 19.3
+  //   lm_head TP=1 (1002):      stream-K 188.6, whole tiles 183.7
+  //   lm_head TP=8 (126):       stream-K 36.7, whole tiles 32.4
+  // (and stream-K over whole tiles by 10-12 % for gate/up at TP=1 with 1..64
+  // tokens).  So: the persistent kernel above a quarter tile per SM, one CTA
+  // per SM walking the tiles with the weight stream never drained; stream-K
+  // below 0.6 tiles per SM and between one and three, whole tiles otherwise.
+  // KRT_PROJ_PERSISTENT=0 / 1 and KRT_PROJ_STREAMK=0 / 1 force either choice.
   const int forced = env_int("KRT_PROJ_PERSISTENT", -1);
-  if (forced == 1 || (forced != 0 && 2 * tiles > device_sm_count())) {
+  const int sk_forced = env_int("KRT_PROJ_STREAMK", -1);
+  const bool sk_possible = p.sk_part != nullptr && sk_forced != 0;  // the workspace holds the partials
+  const bool sk_auto = 10 * tiles < 6 * sms || (tiles >= sms && tiles < 3 * sms);
+  if (forced == 1 || (forced != 0 && (2 * tiles > sms || (4 * tiles > sms && sk_possible)))) {
     const size_t budget = smem_cap_bytes() - proj_persistent_smem_bytes(0, 1, p.n_pad);
     int kc = env_int("KRT_PROJ_KC", 2) == 1 ? 1 : 2;
     if (num_kb % 2 != 0 || budget / (2 * (16384 + (size_t)p.n_pad * 128)) < 3) kc = 1;
@@ -475,6 +490,7 @@ int run_projection(PagedParams& p, const void* weight, int weight_rows, const ch
       p.stages = stages;
       p.splits = 1;
       p.prefetch = env_int("KRT_L2_PREFETCH_STAGES", 0);
+      p.sk = sk_possible && (sk_forced == 1 || sk_auto) ? 1 : 0;
       int cols = 32;
       while (cols < 2 * p.n_pad) cols <<= 1;
       p.tmem_cols = cols;
@@ -529,6 +545,7 @@ int projection_params(PagedParams& p, const char* name, const void* x, const voi
     return set_error(KRT_ERR_INVALID, "%s: tensors must be 16-byte aligned", name);
   const size_t need = ws_layout(num_tokens, d_model).total;
   if (ws_bytes < need) return set_error(KRT_ERR_WORKSPACE, "%s: workspace of %zu bytes, %zu needed", name, ws_bytes, need);
+  const ProjWsLayout PL = proj_ws_layout(num_tokens, d_model);
   std::memset(&p, 0, sizeof(p));
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.gamma = static_cast<const __nv_bfloat16*>(gamma);
@@ -543,6 +560,13 @@ int projection_params(PagedParams& p, const char* name, const void* x, const voi
   p.tok_pos = reinterpret_cast<int*>(ws + L.pos_off);
   p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
   p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
+  // a workspace of krt_projection_workspace_size() bytes also holds the
+  // stream-K flags and partials; a smaller one (the base layout) keeps the
+  // persistent kernel on whole tiles
+  if (ws_bytes >= PL.total) {
+    p.sk_flags = reinterpret_cast<int*>(ws + PL.flags_off);
+    p.sk_part = reinterpret_cast<float*>(ws + PL.part_off);
+  }
   return KRT_OK;
 }
 
@@ -550,7 +574,7 @@ int projection_params(PagedParams& p, const char* name, const void* x, const voi
 
 extern "C" size_t krt_projection_workspace_size(int32_t num_tokens, int32_t d_model) {
   if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0) return 0;
-  return ws_layout(num_tokens, d_model).total;
+  return proj_ws_layout(num_tokens, d_model).total;
 }
 
 extern "C" int krt_gate_up_swiglu(const krt_gate_up_args* a, void* stream) {

@@ -469,7 +469,12 @@ int gemm_stages(int tile_m, int n_pad, int kc, int splits) {
 }
 
 // Box depth with the most weight bytes in flight, leaving every split at
-// least one box of the K range.
+// least one box of the K range; a 64-column box gives way to a 128-column
+// one that still double-buffers and keeps two thirds of its bytes in
+// flight, because one box costs an mbarrier round trip and an MMA issue
+// either way (B200, 128 tokens, 4 splits: K = 14336 -> 4096 down projection
+// 33.2 us with 64-column boxes in 5 stages, 31.3 us with 128-column boxes
+// in 2; K = 4096 o projection 15.1 -> 13.8 us).
 int gemm_kc(int tile_m, int num_kb, int n_pad, int splits) {
   const int forced = env_int_value("KRT_GEMM_KC", 0);  // box depth for tuning
   if ((forced == 1 || forced == 2 || forced == 4) && num_kb % forced == 0 && num_kb / forced >= splits &&
@@ -484,6 +489,10 @@ int gemm_kc(int tile_m, int num_kb, int n_pad, int splits) {
       best_bytes = bytes;
       best = kc;
     }
+  }
+  if (best == 1 && num_kb % 2 == 0 && num_kb / 2 >= splits) {
+    const int st2 = gemm_stages(tile_m, n_pad, 2, splits);
+    if (st2 >= 2 && (size_t)st2 * 2 * tile_m * 128 * 3 >= best_bytes * 2) best = 2;
   }
   return best;
 }
@@ -535,6 +544,52 @@ GemmCfg gemm_config(int n_out, int num_kb, int n_pad, int world) {
   return cfg;
 }
 
+// Large token counts without the fused exchange (one GPU, or the NCCL route):
+// the persistent projection kernel over 256-token blocks (tile = 128 output
+// features x 256 tokens, row tiles fastest, UMMA N = 256, two TMEM
+// accumulators), y = bf16(x W^T + residual).  The 256-token slices of the
+// decode-shaped kernel re-stream the whole weight shard per slice; here the
+// CTAs of one round walk W together and share it through L2.  Taken when the
+// tiles fill the SMs (KRT_GEMM_LARGE_T=0 keeps the slices).
+bool gemm_large_t_eligible(const krt_gemm_ar_args* a) {
+  if (a->num_tokens <= 256 || env_int_value("KRT_GEMM_LARGE_T", 1) == 0) return false;
+  const long long tiles = (long long)(a->n_out / 128) * ((a->num_tokens + 255) / 256);
+  return tiles >= device_sm_count();
+}
+
+int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, int* status, cudaStream_t s) {
+  PagedParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.num_tokens = a->num_tokens;
+  q.n_pad = 256;
+  q.d_model = a->k_local;
+  q.status = status;
+  q.epi = kEpiStore;
+  q.y = static_cast<__nv_bfloat16*>(a->y);
+  q.y_stride = a->y_stride;
+  q.residual = static_cast<const __nv_bfloat16*>(residual);
+  q.row_tiles = a->n_out / 128;
+  const size_t cap = (size_t)env_int_value("KRT_SMEM_CAP_KB", 227) * 1024;
+  const size_t budget = cap - proj_persistent_smem_bytes(0, 1, q.n_pad);
+  const size_t stage1 = 16384 + (size_t)q.n_pad * 128;
+  q.kc = (a->k_local / 64) % 2 == 0 && budget / (2 * stage1) >= 3 ? 2 : 1;
+  q.stages = (int)(budget / (q.kc * stage1));
+  if (q.stages > 8) q.stages = 8;
+  if (q.stages < 2) return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: shared memory too small");
+  q.tmem_cols = 512;
+  CUtensorMap tmap_w, tmap_x;
+  int rc = make_tmap_bf16_3d(&tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local, (uint64_t)a->k_local, 128,
+                             (uint32_t)q.kc);
+  if (rc) return rc;
+  rc = make_tmap_bf16_3d(&tmap_x, a->x, (uint64_t)a->num_tokens, (uint64_t)a->k_local, (uint64_t)a->x_stride, 256,
+                         (uint32_t)q.kc);
+  if (rc) return rc;
+  const int tiles = q.row_tiles * ((a->num_tokens + 255) / 256);
+  cudaError_t e = launch_proj_persistent(tmap_w, tmap_x, q, tiles, s);
+  if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
+  return KRT_OK;
+}
+
 }  // namespace
 
 extern "C" size_t krt_rowparallel_gemm_ar_workspace_size(void) { return kWsHeaderBytes; }
@@ -581,6 +636,16 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
   if (a->residual && (reinterpret_cast<uintptr_t>(a->residual) & 15))
     return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: residual must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
+  if (p.comm.world == 1 && gemm_large_t_eligible(a)) {
+    int rc = gemm_large_t(a, residual, p.status, s);
+    if (rc) return rc;
+    if (via_nccl) {
+      ncclResult_t r = nccl_api().all_reduce(a->y, a->y, (size_t)a->num_tokens * a->n_out, ncclBfloat16, ncclSum,
+                                             c->nccl, s);
+      if (r != ncclSuccess) return nccl_error(r, "krt_rowparallel_gemm_ar: ncclAllReduce");
+    }
+    return clear_error();
+  }
   // Every slice's parameters and tensor maps are built before the first
   // launch: with a communicator, every rank must make the same launches (the
   // exchange epochs count them), so a call that fails on the host fails

@@ -18,10 +18,35 @@
 //     lane r parks its 16 values token-major in the group's buffer, then
 //     thread (token j, rows 16 g .. 16 g + 15) applies the epilogue with the
 //     partner rows 16 (g ^ 4) .. (the same scheme as the prefill kernel).
+// Work split.  Tile-granular (p.sk == 0): CTA c takes tiles c, c + G, ...
+// (G = gridDim.x), full K each.  With T tiles not a multiple of G the last
+// round leaves SMs idle (B200, gate/up at TP=1: 224 tiles on 148 SMs, the
+// SMs busy 72 % of the kernel).  Stream-K (p.sk != 0): the T x KB k-boxes
+// are cut into G equal runs, run c = boxes [c T KB / G, (c+1) T KB / G) in
+// (tile, k) order, so every SM streams the same number of weight bytes.  A
+// run is a list of segments (tile, k0, k1):
+//   * k0 == 0 and k1 == KB: a whole tile, epilogue as usual;
+//   * k0 > 0 (only a run's first segment): the tail of a tile another CTA
+//     started.  The epilogue stores the raw fp32 accumulator to
+//     sk_part[c] and releases sk_flags[c];
+//   * k0 == 0 and k1 < KB (only a run's last segment): the head of a tile
+//     that continues in runs c + 1, c + 2, ...  The epilogue acquires their
+//     flags (bounded wait, status bit 64 when it runs out), adds their
+//     partials in run order and applies the epilogue; then it clears the
+//     flags for the next launch.
+// A head waits only for runs that start with their tile, i.e. at the
+// beginning of those CTAs' work, while the head comes at the end of its own:
+// all G CTAs are resident together (one per SM, G <= #SMs), and the
+// dependent kernel cannot take an SM before every CTA here has started.
+// Token blocks (p.row_tiles > 0, more than 256 tokens): tile = tb * row_tiles
+// + rt covers weight rows 128 rt .. and tokens n_pad tb .. (n_pad = 256); row
+// tiles run fastest, so the CTAs of one round share a few token blocks of X
+// and walk W in step (both kept in L2 with an evict-last policy).
 // Epilogues (PagedParams::epi): kEpiSwiglu (act = silu(gate) * up, gate and
-// up rows side by side in 64-row groups) and kEpiArgmax (the CTA keeps each
+// up rows side by side in 64-row groups), kEpiArgmax (the CTA keeps each
 // token's best (logit, index) over all its tiles in shared memory and folds
-// it into the global keys once at the end).  The kEpiQkv branch (bias, RoPE,
+// it into the global keys once at the end; one token block) and kEpiStore
+// (y = bf16(acc + residual): the row-parallel GEMM at large token counts).  The kEpiQkv branch (bias, RoPE,
 // Q out, K/V into the pool) mirrors the prefill kernel's epilogue; the
 // launcher does not offer it (QKV runs on the split-K decode kernel).
 #include <cstdint>
@@ -79,10 +104,32 @@ __global__ void __launch_bounds__(kPjThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_kc = p.d_model / (kBK * KC);
-  const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total = my_tiles * num_kc;  // pipeline stages this CTA streams
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  // this CTA's k-boxes: [box0, box0 + total) of the (tile, k) order (stream-K),
+  // or its tiles' boxes one after another (tile-granular)
+  const long long all_boxes = (long long)num_tiles * num_kc;
+  const long long box0 = p.sk ? all_boxes * c / G : 0;
+  const int my_tiles = c < num_tiles ? (num_tiles - 1 - c) / G + 1 : 0;
+  const int total = p.sk ? (int)(all_boxes * (c + 1) / G - box0) : my_tiles * num_kc;
   const int pre = total < S ? total : S;
-  auto tile_of = [&](int it) { return (int)blockIdx.x + (it / num_kc) * (int)gridDim.x; };
+  auto tile_of = [&](int it) {
+    return p.sk ? (int)((box0 + it) / num_kc) : c + (it / num_kc) * G;
+  };
+  auto kb_of = [&](int it) { return p.sk ? (int)((box0 + it) % num_kc) : it % num_kc; };
+  // segments: (tile, k0, k1); tile-granular runs have my_tiles whole tiles
+  const int first_tile = p.sk ? (int)(box0 / num_kc) : c;
+  const int num_segs = p.sk ? (total > 0 ? tile_of(total - 1) - first_tile + 1 : 0) : my_tiles;
+  auto seg_tile = [&](int i) { return p.sk ? first_tile + i : c + i * G; };
+  auto seg_k0 = [&](int i) { return (p.sk && i == 0) ? (int)(box0 - (long long)first_tile * num_kc) : 0; };
+  auto seg_k1 = [&](int i) {
+    if (!p.sk) return num_kc;
+    const long long end = box0 + total - (long long)seg_tile(i) * num_kc;
+    return end < num_kc ? (int)end : num_kc;
+  };
+  // tile -> (weight row tile, token block)
+  const int RT = p.row_tiles > 0 ? p.row_tiles : num_tiles;
+  auto w_row = [&](int tile) { return (tile % RT) * 128; };
+  auto x_row = [&](int tile) { return (tile / RT) * n_pad; };
 
   uint64_t pol_w = 0;
   if (threadIdx.x == 0) {
@@ -98,15 +145,15 @@ __global__ void __launch_bounds__(kPjThreads, 1)
     fence_mbar_init();
     // the first stages' weight tiles depend on nothing: request them now
     tma_prefetch_desc(&tmap_w);
-    pol_w = make_l2_policy_evict_first();  // weights are streamed once
+    // weights are streamed once, unless several token blocks re-read them
+    pol_w = RT < num_tiles ? make_l2_policy_evict_last() : make_l2_policy_evict_first();
     for (int it = 0; it < pre; ++it) {
       mbar_arrive_expect_tx(&tl->full[it], stage_bytes);
-      tma_load_3d(a_smem + (size_t)it * a_stage, &tmap_w, &tl->full[it], 0, tile_of(it) * 128, (it % num_kc) * KC,
-                  pol_w);
+      tma_load_3d(a_smem + (size_t)it * a_stage, &tmap_w, &tl->full[it], 0, w_row(tile_of(it)), kb_of(it) * KC, pol_w);
     }
     // optionally the next p.prefetch stages' weights into L2 beyond the ring
     for (int it = pre; it < total && it < pre + p.prefetch; ++it)
-      tma_prefetch_l2_3d(&tmap_w, 0, tile_of(it) * 128, (it % num_kc) * KC);
+      tma_prefetch_l2_3d(&tmap_w, 0, w_row(tile_of(it)), kb_of(it) * KC);
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
@@ -128,7 +175,8 @@ __global__ void __launch_bounds__(kPjThreads, 1)
       const uint64_t pol_x = make_l2_policy_evict_last();  // x_hat is re-read by every tile
       pdl_wait();  // x_hat comes from the prep kernel
       for (int it = 0; it < pre; ++it)
-        tma_load_3d(b_smem + (size_t)it * b_stage, &tmap_x, &tl->full[it], 0, 0, (it % num_kc) * KC, pol_x);
+        tma_load_3d(b_smem + (size_t)it * b_stage, &tmap_x, &tl->full[it], 0, x_row(tile_of(it)), kb_of(it) * KC,
+                    pol_x);
       for (int it = pre; it < total; ++it) {
         const int s = it % S;
         const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -137,11 +185,11 @@ __global__ void __launch_bounds__(kPjThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&tl->full[s], stage_bytes);
-        tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, tile_of(it) * 128, (it % num_kc) * KC,
-                    pol_w);
-        tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (it % num_kc) * KC, pol_x);
+        const int tile = tile_of(it);
+        tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, w_row(tile), kb_of(it) * KC, pol_w);
+        tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, x_row(tile), kb_of(it) * KC, pol_x);
         const int pf = it + p.prefetch;
-        if (p.prefetch > 0 && pf < total) tma_prefetch_l2_3d(&tmap_w, 0, tile_of(pf) * 128, (pf % num_kc) * KC);
+        if (p.prefetch > 0 && pf < total) tma_prefetch_l2_3d(&tmap_w, 0, w_row(tile_of(pf)), kb_of(pf) * KC);
       }
     }
   } else if (warp == 1) {
@@ -150,7 +198,7 @@ __global__ void __launch_bounds__(kPjThreads, 1)
       const uint32_t idesc = umma_idesc_bf16(128, n_pad);
       int it = 0;
       bool alive = true;
-      for (int local = 0; local < my_tiles && alive; ++local) {
+      for (int local = 0; local < num_segs && alive; ++local) {
         const uint32_t buf = (uint32_t)local & 1u;
         const uint32_t use = (uint32_t)local >> 1;
         if (!mbar_wait(&tl->tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
@@ -159,7 +207,8 @@ __global__ void __launch_bounds__(kPjThreads, 1)
         }
         tc_fence_after();
         const uint32_t dcol = tmem_base + buf * (uint32_t)n_pad;
-        for (int kb = 0; kb < num_kc; ++kb, ++it) {
+        const int k0 = seg_k0(local), k1 = seg_k1(local);
+        for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (uint32_t)(it / S) & 1u;
           if (!mbar_wait(&tl->full[s], ph, abort_flag)) {
@@ -173,7 +222,7 @@ __global__ void __launch_bounds__(kPjThreads, 1)
             const uint64_t bd = umma_desc_sw128(smem_u32(b_smem + (size_t)s * b_stage + (size_t)kc * b_chunk));
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_bf16(dcol, ad + 2u * kk, bd + 2u * kk, idesc, (kb > 0 || kc > 0 || kk > 0) ? 1u : 0u);
+              umma_bf16(dcol, ad + 2u * kk, bd + 2u * kk, idesc, (kb > k0 || kc > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&tl->empty[s]);
         }
@@ -190,10 +239,19 @@ __global__ void __launch_bounds__(kPjThreads, 1)
     const int j = gt & 15, g8 = gt >> 4;
     const int bar_grp = 1 + grp;        // 128-thread barrier of this group
     float* ybuf = ybufs + grp * kPjYBufFloats;
-    const int T = p.num_tokens;
     pdl_wait();
-    for (int local = 0; local < my_tiles; ++local) {
-      const int tile = (int)blockIdx.x + local * (int)gridDim.x;
+    for (int local = 0; local < num_segs; ++local) {
+      const int tile = seg_tile(local);
+      const int t_base = x_row(tile);  // first token of the tile's block
+      const int T = p.num_tokens - t_base < n_pad ? p.num_tokens - t_base : n_pad;
+      const int k0 = seg_k0(local), k1 = seg_k1(local);
+      const bool tail = k0 > 0;                  // partial for the CTA that holds k-box 0
+      const bool head = k0 == 0 && k1 < num_kc;  // add the partials of runs c + 1, ...
+      int partners = 0;                          // runs that continue this tile
+      if (head) {
+        const long long tile_end = (long long)(tile + 1) * num_kc;
+        while (c + 1 + partners < G && all_boxes * (c + 1 + partners) / G < tile_end) ++partners;
+      }
       const uint32_t buf = (uint32_t)local & 1u;
       const uint32_t use = (uint32_t)local >> 1;
       if (EPI == kEpiQkv && local == 0) {
@@ -206,8 +264,31 @@ __global__ void __launch_bounds__(kPjThreads, 1)
       const bool waited = mbar_wait_warp(&tl->tmem_full[buf], use & 1u, abort_flag);
       if (!waited && lane == 0) pj_fail(p, tl, kStatusTimeoutAccum);
       tc_fence_after();
-      if (named_bar_any(3, 256, !waited || *abort_flag != 0)) break;
+      bool got = true;
+      if (head && ept == 0) {
+        for (int q = 1; q <= partners && got; ++q) got = wait_flag_gpu(reinterpret_cast<const uint32_t*>(p.sk_flags + c + q), 1u);
+        if (!got) pj_fail(p, tl, kStatusTimeoutCluster);
+      }
+      if (named_bar_any(3, 256, !waited || !got || *abort_flag != 0)) break;
       const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16) + buf * (uint32_t)n_pad;
+      if (tail) {
+        // the raw accumulator to this run's partial slot, token-major
+        float* part = p.sk_part + (size_t)c * n_pad * 128 + r;
+        for (int c0 = grp * 16; c0 < n_pad && c0 < T; c0 += 32) {
+          float acc[16];
+          tmem_ld16(taddr + (uint32_t)c0, acc);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) __stcg(part + (size_t)(c0 + i) * 128, acc[i]);
+        }
+        tc_fence_before();
+        named_bar_sync(3, 256);
+        if (ept == 0) {
+          __threadfence();
+          st_release_gpu(reinterpret_cast<uint32_t*>(p.sk_flags + c), 1u);
+        }
+        if (lane == 0) mbar_arrive(&tl->tmem_empty[buf]);
+        continue;
+      }
       const float bias_r = EPI == kEpiQkv && p.bias ? __bfloat162float(p.bias[tile * kHeadDim + r]) : 0.f;
       const bool rot = EPI == kEpiQkv ? tile < p.n_heads + p.n_kv_heads : (EPI == kEpiSwiglu ? g8 < 4 : false);
       for (int c0 = grp * 16; c0 < n_pad; c0 += 32) {
@@ -218,6 +299,11 @@ __global__ void __launch_bounds__(kPjThreads, 1)
         if (EPI == kEpiQkv && rot) load_rope_n<16>(p, pos, 16 * g8, cs, sn);
         float acc[16];
         tmem_ld16(taddr + (uint32_t)c0, acc);
+        for (int q = 1; q <= partners; ++q) {
+          const float* part = p.sk_part + (size_t)(c + q) * n_pad * 128 + r;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[i] += __ldcg(part + (size_t)(c0 + i) * 128);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) ybuf[i * kYStride + r] = acc[i] + bias_r;
         named_bar_sync(bar_grp, 128);
@@ -227,6 +313,28 @@ __global__ void __launch_bounds__(kPjThreads, 1)
           if (rot) ld_smem_16f(ybuf + j * kYStride + 16 * (g8 ^ 4), yp);
           if (EPI == kEpiQkv) {
             store_rows_n<16>(p, tile, t, 16 * g8, g8 < 4 ? -1.f : 1.f, pos, tl->slot[t], y, yp, cs, sn);
+          } else if (EPI == kEpiStore) {
+            const size_t off = (size_t)(t_base + t) * p.y_stride + w_row(tile) + 16 * g8;
+            if (p.residual) {
+              const uint4* res = reinterpret_cast<const uint4*>(p.residual + off);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 v = res[h];
+                const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float2 f = __bfloat1622float2(b2[q]);
+                  y[8 * h + 2 * q] += f.x;
+                  y[8 * h + 2 * q + 1] += f.y;
+                }
+              }
+            }
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
+            uint4* dst = reinterpret_cast<uint4*>(p.y + off);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
           } else if (EPI == kEpiSwiglu) {
             if (g8 < 4) {
               uint32_t w[8];
@@ -236,7 +344,8 @@ __global__ void __launch_bounds__(kPjThreads, 1)
                 const float a1 = y[2 * i + 1] / (1.f + __expf(-y[2 * i + 1])) * yp[2 * i + 1];
                 w[i] = pack_bf16x2(a0, a1);
               }
-              uint4* dst = reinterpret_cast<uint4*>(p.act + (size_t)t * p.act_stride + (size_t)tile * 64 + 16 * g8);
+              uint4* dst = reinterpret_cast<uint4*>(p.act + (size_t)(t_base + t) * p.act_stride +
+                                                    (size_t)(tile % RT) * 64 + 16 * g8);
               dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
               dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
             }
@@ -244,7 +353,7 @@ __global__ void __launch_bounds__(kPjThreads, 1)
             unsigned long long best = 0ull;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const int row = tile * 128 + 16 * g8 + i;
+              const int row = w_row(tile) + 16 * g8 + i;
               if (row < p.vocab_valid) {
                 const unsigned long long k = argmax_key(y[i], (uint32_t)(p.vocab_offset + row));
                 best = k > best ? k : best;
@@ -258,10 +367,12 @@ __global__ void __launch_bounds__(kPjThreads, 1)
       tc_fence_before();
       named_bar_sync(3, 256);  // both groups are done with this tile's accumulator
       if (lane == 0) mbar_arrive(&tl->tmem_empty[buf]);
+      // the partials are consumed: clear their flags for the next launch
+      if (ept < partners) p.sk_flags[c + 1 + ept] = 0;
     }
     if (EPI == kEpiArgmax) {
       named_bar_sync(3, 256);
-      for (int t = ept; t < T; t += 256)
+      for (int t = ept; t < p.num_tokens; t += 256)
         if (tl->key[t] != 0ull) atomicMax(p.keys + t, tl->key[t]);
     }
   }
@@ -282,7 +393,13 @@ static cudaError_t launch_pj_t(const CUtensorMap& tmap_w, const CUtensorMap& tma
       cudaFuncSetAttribute(proj_persistent_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int grid = device_sm_count();
-  if (grid > num_tiles) grid = num_tiles;
+  if (p.sk) {
+    const long long boxes = (long long)num_tiles * (p.d_model / (kBK * p.kc));
+    if (grid > kSkMaxCtas) grid = kSkMaxCtas;
+    if (grid > boxes) grid = (int)boxes;
+  } else if (grid > num_tiles) {
+    grid = num_tiles;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kPjThreads, 1, 1);
@@ -300,6 +417,7 @@ cudaError_t launch_proj_persistent(const CUtensorMap& tmap_w, const CUtensorMap&
                                    int num_tiles, cudaStream_t stream) {
   if (p.epi == kEpiSwiglu) return launch_pj_t<kEpiSwiglu>(tmap_w, tmap_x, p, num_tiles, stream);
   if (p.epi == kEpiArgmax) return launch_pj_t<kEpiArgmax>(tmap_w, tmap_x, p, num_tiles, stream);
+  if (p.epi == kEpiStore) return launch_pj_t<kEpiStore>(tmap_w, tmap_x, p, num_tiles, stream);
   return cudaErrorInvalidValue;  // the QKV projection runs on the split-K decode kernel
 }
 

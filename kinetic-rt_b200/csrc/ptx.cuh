@@ -21,7 +21,7 @@ enum : int {
   kStatusBadBlock = 8,        // paged scatter: block id / position outside the pool
   kStatusTimeoutPeer = 16,    // cross-GPU flag wait ran out
   kStatusBadSplit = 32,       // split-K bookkeeping inconsistent
-  kStatusTimeoutCluster = 64, // partials from the other CTAs of the cluster did not arrive
+  kStatusTimeoutCluster = 64, // split-K partials of the other CTAs (cluster or stream-K runs) did not arrive
 };
 
 // Wall-clock budget for any single wait: 2 s.
@@ -404,6 +404,25 @@ __device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t exp
     if (ld_acquire_sys(flag) == expect) return true;
     if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
     __nanosleep(64);
+  }
+}
+
+// The same between CTAs of one GPU (device scope).
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool wait_flag_gpu(const uint32_t* flag, uint32_t expect) {
+  if (ld_acquire_gpu(flag) == expect) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (ld_acquire_gpu(flag) == expect) return true;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+    __nanosleep(32);
   }
 }
 

@@ -51,6 +51,19 @@ struct PagedParams {
   unsigned long long* keys;  // kEpiArgmax: [num_tokens] packed (logit, index) maxima
   int vocab_valid;      // kEpiArgmax: weight rows that are real vocabulary entries
   int vocab_offset;     // kEpiArgmax: vocabulary index of weight row 0
+  // Persistent projection kernel, stream-K work split (sk != 0): every CTA
+  // takes an equal run of (tile, k-box) work; a CTA whose run starts inside
+  // a tile leaves its fp32 partial in sk_part[cta] and raises sk_flags[cta],
+  // and the CTA holding that tile's first k-box adds it before the epilogue.
+  int sk;
+  int* sk_flags;        // [kSkMaxCtas] 0 / 1, back to 0 once consumed
+  float* sk_part;       // [kSkMaxCtas][n_pad][128] fp32 partials
+  // Persistent projection kernel over token blocks of n_pad tokens:
+  // tile = block * row_tiles + row tile (row_tiles 0: one token block).
+  int row_tiles;
+  __nv_bfloat16* y;     // kEpiStore: [num_tokens, y_stride] bf16(acc + residual)
+  int y_stride;
+  const __nv_bfloat16* residual;  // kEpiStore: optional, same layout as y
 };
 
 // Epilogues of the decode-shaped (swap-AB, split-K) projection kernel:
@@ -59,7 +72,9 @@ struct PagedParams {
 //               act[t, f + i] = silu(gate) * up
 //   kEpiArgmax  logits of a vocabulary shard: per token the largest logit
 //               and its index, folded into keys[t] with atomicMax
-enum : int { kEpiQkv = 0, kEpiSwiglu = 1, kEpiArgmax = 2 };
+//   kEpiStore   y[t, row] = bf16(acc + residual[t, row]) (persistent kernel,
+//               the row-parallel GEMM at large token counts)
+enum : int { kEpiQkv = 0, kEpiSwiglu = 1, kEpiArgmax = 2, kEpiStore = 3 };
 
 // Orderable 64-bit key of (logit, vocabulary index): larger logits give
 // larger keys, and for equal logits the smaller index gives the larger key
@@ -89,6 +104,25 @@ inline WsLayout ws_layout(int T, int D) {
   l.slot_off = up(l.pos_off + 4 * (size_t)T);
   l.xhat_off = up(l.slot_off + 8 * (size_t)T);
   l.total = up(l.xhat_off + 2 * (size_t)T * D);
+  return l;
+}
+
+// Projection workspace: the layout above, then the stream-K flags and
+// partials of the persistent projection kernel (at most kSkMaxCtas CTAs,
+// one 128-row partial of n_pad tokens each).
+constexpr int kSkMaxCtas = 160;
+struct ProjWsLayout {
+  WsLayout base;
+  size_t flags_off, part_off, total;
+};
+inline ProjWsLayout proj_ws_layout(int T, int D) {
+  auto up = [](size_t v) { return (v + 1023) & ~size_t(1023); };
+  ProjWsLayout l;
+  l.base = ws_layout(T, D);
+  const size_t n_pad = ((size_t)T + 15) / 16 * 16;
+  l.flags_off = l.base.total;
+  l.part_off = up(l.flags_off + 4 * (size_t)kSkMaxCtas);
+  l.total = up(l.part_off + (size_t)kSkMaxCtas * n_pad * 128 * 4);
   return l;
 }
 

@@ -33,14 +33,29 @@ def dev(torch, a):
     return torch.from_numpy(f32_to_bf16_bits(a).view(np.int16)).view(torch.bfloat16).cuda()
 
 
-@pytest.mark.parametrize("persistent,T,I", [("0", 37, 320), ("1", 37, 320), ("auto", 128, 9600), ("1", 200, 704)])
-def test_gate_up_swiglu(torch_cuda, monkeypatch, persistent, T, I):
-    """Split-K kernel (few tiles) and the persistent kernel (many tiles: 150
-    tiles on 148 SMs gives two tiles to some CTAs, through both TMEM buffers)."""
+def _projection_kernel(monkeypatch, mode):
+    """splitk: the split-K decode kernel; tiles: the persistent kernel on whole
+    tiles; streamk: the persistent kernel on equal runs of k-boxes; auto: the
+    launcher's choice."""
+    if mode == "splitk":
+        monkeypatch.setenv("KRT_PROJ_PERSISTENT", "0")
+    elif mode in ("tiles", "streamk"):
+        monkeypatch.setenv("KRT_PROJ_PERSISTENT", "1")
+        monkeypatch.setenv("KRT_PROJ_STREAMK", "1" if mode == "streamk" else "0")
+
+
+@pytest.mark.parametrize("mode,T,I", [("splitk", 37, 320), ("tiles", 37, 320), ("streamk", 37, 320),
+                                      ("auto", 128, 9600), ("tiles", 200, 704), ("streamk", 200, 704),
+                                      ("streamk", 64, 9600)])
+def test_gate_up_swiglu(torch_cuda, monkeypatch, mode, T, I):
+    """Split-K kernel (few tiles) and the persistent kernel: whole tiles (150
+    tiles on 148 SMs gives two tiles to some CTAs, through both TMEM buffers)
+    and stream-K (5 tiles of 4 k-boxes on 20 CTAs: every tile is one head
+    and three partials; 150 tiles on 148 CTAs: runs of 4-5 boxes crossing
+    tile boundaries)."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
-    if persistent != "auto":
-        monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
+    _projection_kernel(monkeypatch, mode)
     rng = np.random.Generator(np.random.PCG64(1))
     D = 512
     x, g = bf(rng, T, D), bf(rng, D, scale=0.1, base=1.0)
@@ -64,15 +79,17 @@ def _check_argmax(logits, idx):
     return np.mean(idx == logits.argmax(-1))
 
 
-@pytest.mark.parametrize("persistent,V0,V1", [("0", 1000, 777), ("1", 1000, 777), ("auto", 40000, 1777)])
-def test_lm_head_argmax_two_shards(torch_cuda, monkeypatch, persistent, V0, V1):
+@pytest.mark.parametrize("mode,V0,V1", [("splitk", 1000, 777), ("tiles", 1000, 777), ("streamk", 1000, 777),
+                                       ("auto", 40000, 1777), ("tiles", 40000, 1777)])
+def test_lm_head_argmax_two_shards(torch_cuda, monkeypatch, mode, V0, V1):
     """Two vocabulary shards (neither a multiple of 128 rows) folded into one
     key array give the argmax over the whole vocabulary; split-K and
-    persistent kernels (313 tiles: three tiles for some CTAs)."""
+    persistent kernels (313 tiles: three tiles for some CTAs on whole tiles;
+    runs crossing tile boundaries on stream-K).  The second shard reuses the
+    workspace, so stream-K flags left raised would show as wrong sums."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
-    if persistent != "auto":
-        monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
+    _projection_kernel(monkeypatch, mode)
     rng = np.random.Generator(np.random.PCG64(2))
     T, D = 19, 256
     x, g = bf(rng, T, D), bf(rng, D, scale=0.1, base=1.0)
@@ -228,13 +245,13 @@ def test_decode_steps_tensor_parallel_match_oracle(torch_cuda):
     mp.spawn(_tp_decoder_worker, args=(2, port), nprocs=2, join=True)
 
 
-@pytest.mark.parametrize("persistent", ["0", "1"])
-def test_decode_steps_match_oracle(torch_cuda, monkeypatch, persistent):
+@pytest.mark.parametrize("mode", ["splitk", "tiles", "streamk"])
+def test_decode_steps_match_oracle(torch_cuda, monkeypatch, mode):
     """Three graph-replayed decode steps of a 2-layer model, 5 sequences at
     ragged positions, against the oracle step by step (the oracle's token is
     fed back on both sides, so a near-tie cannot make the runs diverge);
-    gate/up and lm_head on either projection kernel."""
-    monkeypatch.setenv("KRT_PROJ_PERSISTENT", persistent)
+    gate/up and lm_head on each projection kernel."""
+    _projection_kernel(monkeypatch, mode)
     run_decoder_against_oracle(torch_cuda)
 
 

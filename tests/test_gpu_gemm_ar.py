@@ -57,6 +57,39 @@ def test_gemm_single_gpu(torch_cuda, T, K, N):
     np.testing.assert_allclose(y.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("T,K,N,residual,large", [
+    (512, 7168, 4096, False, "1"),    # down_proj shard at TP2: 64 tiles, the 256-token slices
+    (4096, 4096, 4096, True, "1"),    # o_proj unsharded: 512 tiles of 128 x 256 (persistent)
+    (8192, 1792, 4096, False, "1"),   # down_proj shard at TP8
+    (8192, 14336, 4096, True, "1"),   # down_proj unsharded
+    (4700, 512, 4096, True, "1"),     # o_proj shard at TP8, last token block ragged
+    (4700, 512, 4096, True, "0"),     # the same through the slices (KRT_GEMM_LARGE_T=0)
+])
+def test_gemm_large_token_counts(torch_cuda, monkeypatch, T, K, N, residual, large):
+    """Config-3 token counts on one GPU: y = x W^T (+ residual) against the
+    fp64 product of the same bf16 values on a sample of rows that covers
+    every 256-token block's first and last rows and the ragged tail."""
+    torch = torch_cuda
+    from python.kinetic_rt import _lib
+    monkeypatch.setenv("KRT_GEMM_LARGE_T", large)
+    g = torch.Generator(device="cuda").manual_seed(T + K)
+    xd = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+    wd = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    res = (torch.randn(T, N, generator=g, device="cuda")).to(torch.bfloat16) if residual else None
+    y = torch.full((T, N), 7.0, dtype=torch.bfloat16, device="cuda")
+    ws = torch.zeros(_lib.gemm_ar_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    _lib.rowparallel_gemm_ar(None, _lib.gemm_ar_args(xd, wd, y, ws, residual=res))
+    rc, bits = _lib.read_status(ws)
+    assert rc == 0 and bits == 0
+    rows = sorted({t for b in range(0, T, 256) for t in (b, b + 1, min(b + 255, T - 1))} | {T - 1})
+    idx = torch.tensor(rows, device="cuda")
+    xs = xd[idx].float().cpu().numpy().astype(np.float64)
+    ref = xs @ wd.float().cpu().numpy().astype(np.float64).T
+    if res is not None:
+        ref = ref + res[idx].float().cpu().numpy()
+    np.testing.assert_allclose(y[idx].float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
 @pytest.mark.parametrize("T,K,N", [(33, 1536, 384), (200, 640, 256)])
 def test_gemm_half_height_tiles(torch_cuda, monkeypatch, T, K, N):
     """KRT_GEMM_TILE_M=64 selects 64-row weight tiles (read when a shape is
