@@ -38,6 +38,13 @@ METRIC = "decode tokens/s per box at TP=1/2/4/8; fused QKV+RoPE & GEMM+AR % roof
 HIDDEN, N_HEADS, N_KV, HEAD_DIM, INTER, VOCAB, LAYERS = 4096, 32, 8, 128, 14336, 128256, 32
 BATCH, CTX, BLOCK = 64, 2048, 16              # --workload layer
 STACK_BATCH, PROMPT, GEN_STEPS = 128, 4096, 256  # --workload stack
+# --workload stack --model: (layers, hidden, heads, kv heads, intermediate,
+# decode batch, prompt tokens, greedy steps).  8b = config 4 (the metric's
+# workload); 70b = the decode half of config 5 (batch 256 at context 2048).
+STACK_MODELS = {
+    "8b": (32, 4096, 32, 8, 14336, 128, 4096, 256),
+    "70b": (80, 8192, 64, 8, 28672, 256, 2048, 64),
+}
 L2_BYTES = 126 * 1024 * 1024
 NVLINK_GBS = 770.0  # measured B200 peer-copy bandwidth per direction over NVLink 5 (900 GB/s nominal)
 # allreduce messages (bf16 bytes) from which the NCCL route is taken: set from
@@ -498,16 +505,18 @@ def run_krt(args, rank, world, local_rank):
 
 
 # ------------------------------------------------------------- the stack
-def stack_config(n):
+def stack_config(n, model="8b"):
+    L, D, H, KV, I, B, P, G = STACK_MODELS[model]
+    name = "Llama-3-8B" if model == "8b" else "Llama-3-70B"
     return {
-        "workload": (f"Llama-3-8B-shaped decoder stack (random init), decode batch {STACK_BATCH} at contexts "
-                     f"{PROMPT}..{PROMPT + GEN_STEPS} (prompt K/V synthetic), greedy, TP={n}: per layer fused "
+        "workload": (f"{name}-shaped decoder stack (random init), decode batch {B} at contexts "
+                     f"{P}..{P + G} (prompt K/V synthetic), greedy, TP={n}: per layer fused "
                      "RMSNorm+QKV+RoPE+paged-KV scatter, paged GQA attention, o_proj GEMM+allreduce+residual, "
                      "RMSNorm+gate/up+SwiGLU, down_proj GEMM+allreduce+residual; then RMSNorm+lm_head+argmax and the "
                      "next embedding; one CUDA graph per decode step"),
-        "model": "llama-3-8b-shaped", "layers": LAYERS, "global_batch": STACK_BATCH, "seq_len": PROMPT,
-        "gen_steps": GEN_STEPS, "parallelism": f"tp{n}", "hidden": HIDDEN, "heads": f"{N_HEADS}/{N_KV}x{HEAD_DIM}",
-        "intermediate": INTER, "vocab": VOCAB, "kv_block": BLOCK,
+        "model": f"llama-3-{model}-shaped", "layers": L, "global_batch": B, "seq_len": P,
+        "gen_steps": G, "parallelism": f"tp{n}", "hidden": D, "heads": f"{H}/{KV}x{HEAD_DIM}",
+        "intermediate": I, "vocab": VOCAB, "kv_block": BLOCK,
         "per_box": f"value x {8 // n} (8 / TP replicas on one 8-GPU box)" if 8 % n == 0 else None,
         "l2": "inputs larger than L2: each step streams every layer's weights and the whole KV cache",
     }
@@ -723,11 +732,12 @@ def run_gemm_ar(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def stack_kernel_bytes(world, ctx, batch=STACK_BATCH):
+def stack_kernel_bytes(world, ctx, batch=STACK_BATCH, model="8b"):
     """Algorithmic bytes per launch of each kernel of the decode step (this
     rank's share): every input read once, every output written once."""
-    B, D = batch, HIDDEN
-    hq, hkv, ir = N_HEADS // world, N_KV // world, INTER // world
+    _, D, H, KV, I = STACK_MODELS[model][:5]
+    B = batch
+    hq, hkv, ir = H // world, KV // world, I // world
     vr = -(-VOCAB // world)
     qkv_rows = (hq + 2 * hkv) * HEAD_DIM
     return {
@@ -744,9 +754,27 @@ def stack_kernel_bytes(world, ctx, batch=STACK_BATCH):
     }
 
 
+def stack_fits(model, world, gpu_bytes=180e9):
+    """Weights + KV pools of one rank against one GPU's memory (the 70B
+    stack needs TP >= 2)."""
+    L, D, H, KV, I, B, P, G = STACK_MODELS[model]
+    weights = L * (((H + 2 * KV) * HEAD_DIM * D + D * H * HEAD_DIM + 3 * D * I) * 2 // world) \
+        + (VOCAB * D * 2 // world) + VOCAB * D * 2
+    kv = L * B * (P + G + 96) * 2 * (KV // world) * HEAD_DIM * 2
+    return weights + kv < 0.85 * gpu_bytes, weights + kv
+
+
 def run_stack(args, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
+    fits, need = stack_fits(args.model, world)
+    if not fits:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": None, "unit": "decode tokens/s", "n_gpus": world,
+                              "config": stack_config(world, args.model),
+                              "unavailable": f"weights + KV of one rank ({need / 1e9:.0f} GB) exceed one GPU; "
+                                             f"run the {args.model} stack at a higher TP"}), flush=True)
+        return
     comm = None
     if world > 1:
         import datetime
@@ -754,25 +782,27 @@ def run_stack(args, rank, world, local_rank):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
                                 timeout=datetime.timedelta(seconds=120))
         from python.kinetic_rt.dist import TPComm
-        comm = TPComm(rank, world, max_n_out=HIDDEN)
+        comm = TPComm(rank, world, max_n_out=STACK_MODELS[args.model][1])
         comm.attach_nccl(NCCL_THRESHOLD)
-    from python.kinetic_rt.decoder import LLAMA3_8B, PagedDecoder, RankWeights
+    from python.kinetic_rt.decoder import LLAMA3_8B, LLAMA3_70B, PagedDecoder, RankWeights
+    model = args.model
+    shape = LLAMA3_8B if model == "8b" else LLAMA3_70B
+    n_layers, _, _, _, _, B, prompt, gen_steps = STACK_MODELS[model]
     parity = tp_parity_check(torch, comm, rank, world)
-    config3 = gemm_ar_sweep(torch, comm, rank, world) if world > 1 else None
+    config3 = gemm_ar_sweep(torch, comm, rank, world) if world > 1 and model == "8b" else None
     K, W = args.steps, args.warmup
-    B = STACK_BATCH
     # the position the first warm-up step processes: the timed steps sit in
-    # the middle of the GEN_STEPS greedy steps after the prompt
-    first = PROMPT + max(0, (GEN_STEPS - K) // 2 - W)
+    # the middle of the greedy steps after the prompt
+    first = prompt + max(0, (gen_steps - K) // 2 - W)
     e2e_steps = min(K, 64)
-    max_len = max(PROMPT + GEN_STEPS, first + 1 + W + K + e2e_steps + 8)
-    weights = RankWeights.random(torch, LLAMA3_8B, rank, world, seed=0)
-    dec = PagedDecoder(torch, LLAMA3_8B, weights, B, max_len, comm, rank, world)
+    max_len = max(prompt + gen_steps, first + 1 + W + K + e2e_steps + 8)
+    weights = RankWeights.random(torch, shape, rank, world, seed=0)
+    dec = PagedDecoder(torch, shape, weights, B, max_len, comm, rank, world)
     g = torch.Generator(device="cuda").manual_seed(7)
     dec.pools[0].copy_(torch.randn(dec.pools[0].shape, generator=g, device="cuda").to(torch.bfloat16))
     for pool in dec.pools[1:]:
         pool.copy_(dec.pools[0])
-    start = torch.randint(0, VOCAB, (B,), generator=torch.Generator().manual_seed(11))
+    start = torch.randint(0, shape.vocab, (B,), generator=torch.Generator().manual_seed(11))
     dec.start(start, [first] * B)
     graph = dec.capture()  # after one eager step (first calls outside the capture), state restored
     dec.check_status()
@@ -812,7 +842,7 @@ def run_stack(args, rank, world, local_rank):
             traffic = json.load(f)
     except Exception:
         pass
-    kbytes = stack_kernel_bytes(world, ctx_mid)
+    kbytes = stack_kernel_bytes(world, ctx_mid, B, model)
     names = ["qkv_rope_decode", "paged_attention", "o_proj_gemm_ar", "gate_up_swiglu", "down_proj_gemm_ar"]
     kernels = []
 
@@ -834,7 +864,7 @@ def run_stack(args, rank, world, local_rank):
 
     saved_pos = dec.positions.clone()
     for part, name in enumerate(names):
-        us = time_graph(lambda: [dec.layer(li, parts=(part,)) for li in range(LAYERS)], LAYERS, 3)
+        us = time_graph(lambda: [dec.layer(li, parts=(part,)) for li in range(n_layers)], n_layers, 3)
         kernels.append((name, us))
     kernels.append(("lm_head_argmax", time_graph(lambda: _lm(dec), 1, 20)))
     kernels.append(("greedy_step", time_graph(lambda: _greedy(dec), 1, 20)))
@@ -847,9 +877,10 @@ def run_stack(args, rank, world, local_rank):
         ach = nbytes / (us * 1e-6) / 1e9
         entry = {"kernel": name, "bound": "hbm", "us": round(us, 3), "algorithmic_bytes": int(nbytes), "bytes": what,
                  "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-                 "traffic": traffic.get(f"stack_{name}_tp{world}"), "launches_per_step": LAYERS if name in names else 1}
+                 "traffic": traffic.get(f"stack_{name}_tp{world}") if model == "8b" else None,
+                 "launches_per_step": n_layers if name in names else 1}
         if name.endswith("gemm_ar") and world > 1:
-            wire = 2 * (world - 1) / world * B * HIDDEN * 4
+            wire = 2 * (world - 1) / world * B * shape.d_model * 4
             target = max(nbytes / hbm / 1e3, wire / NVLINK_GBS / 1e3)
             entry.update({"nvlink_wire_bytes_per_gpu": int(wire), "roofline_us": round(target, 3),
                           "frac_of_roofline": round(target / us, 4)})
@@ -877,17 +908,18 @@ def run_stack(args, rank, world, local_rank):
     barrier(torch, world)
     e2e_ms = max_over_ranks(torch, e0.elapsed_time(e1), world) / e2e_steps
     dec.check_status()
-    prefill = prefill_entry(torch, rank, world)
+    prefill = prefill_entry(torch, rank, world) if model == "8b" else None
     del graph
     base = None
-    if world == 1:
+    if world == 1 and model == "8b":
         base = cpu_stack_sample()
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "decode tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (random-init weights, random prompt ids and prompt K/V)", "config": stack_config(world),
+            "data": "synthetic (random-init weights, random prompt ids and prompt K/V)",
+            "config": stack_config(world, model),
             "per_box_tokens_per_s": round(value * 8 / world, 1) if 8 % world == 0 else None,
             "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "decode tokens/s",
                     "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4,
@@ -903,7 +935,8 @@ def run_stack(args, rank, world, local_rank):
             "kernels": klist + ([prefill] if prefill else []),
             "parity": parity,
             "config3_gemm_ar": config3,
-            "cpu_baseline": base if base else {"value": None, "note": "timed at N=1 only (rank 0 alone on the host)"},
+            "cpu_baseline": base if base else {"value": None, "note": "timed at N=1 on the 8b stack only (rank 0 "
+                                                                      "alone on the host)"},
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -1241,6 +1274,8 @@ def main():
                          "down_proj_gemm_ar, lm_head_argmax")
     ap.add_argument("--tp", type=int, default=0, help="--workload kernel: TP degree whose shard shapes to use")
     ap.add_argument("--batch", type=int, default=0, help="--workload kernel: tokens per call (default 128)")
+    ap.add_argument("--model", choices=sorted(STACK_MODELS), default="8b",
+                    help="--workload stack: 8b (config 4, the metric's workload) or 70b (config 5's decode half)")
     ap.add_argument("--workload", choices=["stack", "layer", "prefill", "gemm_ar", "kernel"], default="stack",
                     help="stack: decode steps of the Llama-3-8B-shaped stack (default); layer: one decoder layer's "
                          "hot path; prefill: the fused QKV prefill kernel alone")

@@ -74,3 +74,17 @@ def test_stack_config_names_the_metric_workload():
     c = bench.stack_config(8)
     assert c["layers"] == 32 and c["global_batch"] == 128 and c["parallelism"] == "tp8"
     assert "per_box" in c and c["vocab"] == 128256
+
+
+def test_seventy_b_stack_sizes():
+    """Config 5's decode half: 80 layers, hidden 8192, batch 256 at context
+    2048.  Its weights (141 GB) and KV cache (about 172 GB) need TP >= 4 on
+    180 GB GPUs; at TP=8 one step moves about 41 GB per GPU (weight shards
+    17.4 GB, K/V 21.5 GB, activations and the residual stream 2.4 GB)."""
+    c = bench.stack_config(8, "70b")
+    assert c["layers"] == 80 and c["hidden"] == 8192 and c["global_batch"] == 256 and c["seq_len"] == 2048
+    assert not bench.stack_fits("70b", 1)[0] and not bench.stack_fits("70b", 2)[0]
+    assert bench.stack_fits("70b", 8)[0] and bench.stack_fits("8b", 1)[0]
+    kb = bench.stack_kernel_bytes(8, 2048, 256, "70b")
+    per_step = sum(v[0] * (80 if k not in ("lm_head_argmax", "greedy_step") else 1) for k, v in kb.items())
+    assert 40e9 < per_step < 42.5e9
