@@ -545,23 +545,31 @@ GemmCfg gemm_config(int n_out, int num_kb, int n_pad, int world) {
 }
 
 // Large token counts without the fused exchange (one GPU, or the NCCL route):
-// the persistent projection kernel over 256-token blocks (tile = 128 output
-// features x 256 tokens, row tiles fastest, UMMA N = 256, two TMEM
-// accumulators), y = bf16(x W^T + residual).  The 256-token slices of the
-// decode-shaped kernel re-stream the whole weight shard per slice; here the
-// CTAs of one round walk W together and share it through L2.  Taken when the
-// tiles fill the SMs (KRT_GEMM_LARGE_T=0 keeps the slices).
+// the persistent projection kernel over token blocks (tile = 128 output
+// features x 256 tokens, or 128 when 256-token blocks would leave SMs idle;
+// row tiles fastest, two TMEM accumulators), y = bf16(x W^T + residual).  The
+// 256-token slices of the decode-shaped kernel re-stream the whole weight
+// shard per slice; here the CTAs of one round walk W together and share it
+// through L2.  Taken when the tiles cover at least half the SMs
+// (KRT_GEMM_LARGE_T=0 keeps the slices).
+int gemm_large_t_block(const krt_gemm_ar_args* a) {
+  const long long row_tiles = a->n_out / 128, sms = device_sm_count();
+  if (row_tiles * ((a->num_tokens + 255) / 256) >= sms) return 256;
+  return 128;
+}
+
 bool gemm_large_t_eligible(const krt_gemm_ar_args* a) {
   if (a->num_tokens <= 256 || env_int_value("KRT_GEMM_LARGE_T", 1) == 0) return false;
-  const long long tiles = (long long)(a->n_out / 128) * ((a->num_tokens + 255) / 256);
-  return tiles >= device_sm_count();
+  const int bs = gemm_large_t_block(a);
+  const long long tiles = (long long)(a->n_out / 128) * ((a->num_tokens + bs - 1) / bs);
+  return 2 * tiles >= device_sm_count();
 }
 
 int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, int* status, cudaStream_t s) {
   PagedParams q;
   std::memset(&q, 0, sizeof(q));
   q.num_tokens = a->num_tokens;
-  q.n_pad = 256;
+  q.n_pad = gemm_large_t_block(a);
   q.d_model = a->k_local;
   q.status = status;
   q.epi = kEpiStore;
@@ -576,15 +584,15 @@ int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, int* status, c
   q.stages = (int)(budget / (q.kc * stage1));
   if (q.stages > 8) q.stages = 8;
   if (q.stages < 2) return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: shared memory too small");
-  q.tmem_cols = 512;
+  q.tmem_cols = 2 * q.n_pad;
   CUtensorMap tmap_w, tmap_x;
   int rc = make_tmap_bf16_3d(&tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local, (uint64_t)a->k_local, 128,
                              (uint32_t)q.kc);
   if (rc) return rc;
-  rc = make_tmap_bf16_3d(&tmap_x, a->x, (uint64_t)a->num_tokens, (uint64_t)a->k_local, (uint64_t)a->x_stride, 256,
-                         (uint32_t)q.kc);
+  rc = make_tmap_bf16_3d(&tmap_x, a->x, (uint64_t)a->num_tokens, (uint64_t)a->k_local, (uint64_t)a->x_stride,
+                         (uint32_t)q.n_pad, (uint32_t)q.kc);
   if (rc) return rc;
-  const int tiles = q.row_tiles * ((a->num_tokens + 255) / 256);
+  const int tiles = q.row_tiles * ((a->num_tokens + q.n_pad - 1) / q.n_pad);
   cudaError_t e = launch_proj_persistent(tmap_w, tmap_x, q, tiles, s);
   if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
   return KRT_OK;

@@ -234,9 +234,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       pdl_wait();  // X may come from the previous kernel
       for (int i = 0; i < pre; ++i)
         tma_load_3d(b_smem + (size_t)i * b_stage, &tmap_x, &tl->full[i], 0, 0, (kc0 + i) * KC, pol_x);
+      // ring slot and phase advance by increment (no divisions on the issue path)
+      int s = pre % S;
+      uint32_t ph = (uint32_t)(pre / S) & 1u;
       for (int i = pre; i < nk; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
         if (!mbar_wait(&tl->empty[s], ph ^ 1u, abort_flag)) {
           gemm_fail(p, tl, kStatusTimeoutEmpty);
           break;
@@ -245,14 +246,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, row0, (kc0 + i) * KC, pol_w);
         tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, 0, (kc0 + i) * KC, pol_x);
         if (i + p.prefetch < nk) tma_prefetch_l2_3d(&tmap_w, 0, row0, (kc0 + i + p.prefetch) * KC);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(TM, n_pad);
+      int s = 0;
+      uint32_t ph = 0;
       for (int i = 0; i < nk; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
         if (!mbar_wait(&tl->full[s], ph, abort_flag)) {
           gemm_fail(p, tl, kStatusTimeoutFull);
           break;
@@ -267,6 +272,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             umma_bf16(tmem_base, ad + 2u * kk, bd + 2u * kk, idesc, (i > 0 || kc > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&tl->empty[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       umma_commit(&tl->accum);
     }

@@ -174,29 +174,42 @@ __global__ void __launch_bounds__(kPjThreads, 1)
     if (lane == 0) {
       const uint64_t pol_x = make_l2_policy_evict_last();  // x_hat is re-read by every tile
       pdl_wait();  // x_hat comes from the prep kernel
-      for (int it = 0; it < pre; ++it)
-        tma_load_3d(b_smem + (size_t)it * b_stage, &tmap_x, &tl->full[it], 0, x_row(tile_of(it)), kb_of(it) * KC,
-                    pol_x);
-      for (int it = pre; it < total; ++it) {
-        const int s = it % S;
-        const uint32_t ph = (uint32_t)(it / S) & 1u;
-        if (!mbar_wait(&tl->empty[s], ph ^ 1u, abort_flag)) {
-          pj_fail(p, tl, kStatusTimeoutEmpty);
-          break;
+      // The segments' k-boxes in order; the ring slot and its phase advance
+      // by increment (no divisions between a slot turning free and its loads).
+      int it = 0, s = 0;
+      uint32_t ph = 0;
+      bool alive = true;
+      for (int seg = 0; seg < num_segs && alive; ++seg) {
+        const int tile = seg_tile(seg);
+        const int wr = w_row(tile), xr = x_row(tile);
+        const int k1 = seg_k1(seg);
+        for (int kb = seg_k0(seg); kb < k1; ++kb, ++it) {
+          if (it >= pre) {
+            if (!mbar_wait(&tl->empty[s], ph ^ 1u, abort_flag)) {
+              pj_fail(p, tl, kStatusTimeoutEmpty);
+              alive = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&tl->full[s], stage_bytes);
+            tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, wr, kb * KC, pol_w);
+            const int pf = it + p.prefetch;
+            if (p.prefetch > 0 && pf < total) tma_prefetch_l2_3d(&tmap_w, 0, w_row(tile_of(pf)), kb_of(pf) * KC);
+          }
+          // (the first `pre` slots' weight boxes were requested before the wait)
+          tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, xr, kb * KC, pol_x);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-        mbar_arrive_expect_tx(&tl->full[s], stage_bytes);
-        const int tile = tile_of(it);
-        tma_load_3d(a_smem + (size_t)s * a_stage, &tmap_w, &tl->full[s], 0, w_row(tile), kb_of(it) * KC, pol_w);
-        tma_load_3d(b_smem + (size_t)s * b_stage, &tmap_x, &tl->full[s], 0, x_row(tile), kb_of(it) * KC, pol_x);
-        const int pf = it + p.prefetch;
-        if (p.prefetch > 0 && pf < total) tma_prefetch_l2_3d(&tmap_w, 0, w_row(tile_of(pf)), kb_of(pf) * KC);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- UMMA issue
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(128, n_pad);
-      int it = 0;
+      int s = 0;  // ring slot and phase, advanced by increment
+      uint32_t ph = 0;
       bool alive = true;
       for (int local = 0; local < num_segs && alive; ++local) {
         const uint32_t buf = (uint32_t)local & 1u;
@@ -208,9 +221,7 @@ __global__ void __launch_bounds__(kPjThreads, 1)
         tc_fence_after();
         const uint32_t dcol = tmem_base + buf * (uint32_t)n_pad;
         const int k0 = seg_k0(local), k1 = seg_k1(local);
-        for (int kb = k0; kb < k1; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (uint32_t)(it / S) & 1u;
+        for (int kb = k0; kb < k1; ++kb) {
           if (!mbar_wait(&tl->full[s], ph, abort_flag)) {
             pj_fail(p, tl, kStatusTimeoutFull);
             alive = false;
@@ -225,6 +236,10 @@ __global__ void __launch_bounds__(kPjThreads, 1)
               umma_bf16(dcol, ad + 2u * kk, bd + 2u * kk, idesc, (kb > k0 || kc > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&tl->empty[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
         umma_commit(&tl->tmem_full[buf]);
       }

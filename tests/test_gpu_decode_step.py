@@ -153,25 +153,26 @@ def tiny_model(rng, L=2, D=256, H=4, KV=2, I=384, V=1000):
     from python.kinetic_rt.decoder import LlamaShape
     shape = LlamaShape(n_layers=L, d_model=D, n_heads=H, n_kv_heads=KV, inter=I, vocab=V, rope_theta=1e4)
     hd = 128
+    sc = lambda fan_in: min(0.05, fan_in ** -0.5)  # keeps activations O(1) at wide shapes
     full = {k: [] for k in ("qkv", "g_attn", "o", "g_mlp", "gate", "up", "down")}
     for _ in range(L):
-        full["qkv"].append(bf(rng, (H + 2 * KV) * hd, D, scale=0.05))
+        full["qkv"].append(bf(rng, (H + 2 * KV) * hd, D, scale=sc(D)))
         full["g_attn"].append(bf(rng, D, scale=0.1, base=1.0))
-        full["o"].append(bf(rng, D, H * hd, scale=0.05))
+        full["o"].append(bf(rng, D, H * hd, scale=sc(H * hd)))
         full["g_mlp"].append(bf(rng, D, scale=0.1, base=1.0))
-        full["gate"].append(bf(rng, I, D, scale=0.05))
-        full["up"].append(bf(rng, I, D, scale=0.05))
-        full["down"].append(bf(rng, D, I, scale=0.05))
+        full["gate"].append(bf(rng, I, D, scale=sc(D)))
+        full["up"].append(bf(rng, I, D, scale=sc(D)))
+        full["down"].append(bf(rng, D, I, scale=sc(I)))
     full["g_final"] = bf(rng, D, scale=0.1, base=1.0)
-    full["lm_head"] = bf(rng, V, D, scale=0.05)
+    full["lm_head"] = bf(rng, V, D, scale=sc(D))
     full["embed"] = bf(rng, V, D)
     return shape, full
 
 
-def run_decoder_against_oracle(torch, rank=0, world=1, comm=None, steps=3):
+def run_decoder_against_oracle(torch, rank=0, world=1, comm=None, steps=3, model=None):
     from python.kinetic_rt.decoder import PagedDecoder, RankWeights
     rng = np.random.Generator(np.random.PCG64(4))
-    shape, full = tiny_model(rng)
+    shape, full = tiny_model(rng, **(model or {}))
     B, max_len = 5, 80
     w = RankWeights.from_full(torch, shape, full, rank, world)
     dec = PagedDecoder(torch, shape, w, B, max_len, comm=comm, rank=rank, world=world)
@@ -253,6 +254,14 @@ def test_decode_steps_match_oracle(torch_cuda, monkeypatch, mode):
     gate/up and lm_head on each projection kernel."""
     _projection_kernel(monkeypatch, mode)
     run_decoder_against_oracle(torch_cuda)
+
+
+def test_decode_steps_seventy_b_rank_shapes(torch_cuda):
+    """One layer at the shapes one rank of the Llama-3-70B stack holds at
+    TP=8 (hidden 8192, 8 Q heads and 1 KV head, 3584 intermediate features):
+    10 QKV tiles over 128 k-blocks, a single KV head per pool, 8192-wide
+    GEMM outputs; two graph-replayed steps against the oracle."""
+    run_decoder_against_oracle(torch_cuda, steps=2, model=dict(L=1, D=8192, H=8, KV=1, I=3584))
 
 
 def test_runtime_generate_matches_oracle(torch_cuda):

@@ -40,7 +40,7 @@ def torch_cuda():
     (1, 4096, 4096),      # o_proj, one token
     (64, 4096, 4096),     # o_proj, decode batch 64
     (8, 14336, 4096),     # down_proj, unsharded K
-    (300, 1792, 4096),    # down_proj shard at TP8, two 256-token slices
+    (300, 1792, 4096),    # down_proj shard at TP8, 3 blocks of 128 tokens (persistent, ragged last block)
     (17, 512, 256),       # small ragged case
 ])
 def test_gemm_single_gpu(torch_cuda, T, K, N):
@@ -58,7 +58,8 @@ def test_gemm_single_gpu(torch_cuda, T, K, N):
 
 
 @pytest.mark.parametrize("T,K,N,residual,large", [
-    (512, 7168, 4096, False, "1"),    # down_proj shard at TP2: 64 tiles, the 256-token slices
+    (512, 7168, 4096, False, "1"),    # down_proj shard at TP2: 128 tiles of 128 x 128 (persistent)
+    (512, 7168, 4096, True, "0"),     # the same through the 256-token slices (KRT_GEMM_LARGE_T=0)
     (4096, 4096, 4096, True, "1"),    # o_proj unsharded: 512 tiles of 128 x 256 (persistent)
     (8192, 1792, 4096, False, "1"),   # down_proj shard at TP8
     (8192, 14336, 4096, True, "1"),   # down_proj unsharded
@@ -68,7 +69,8 @@ def test_gemm_single_gpu(torch_cuda, T, K, N):
 def test_gemm_large_token_counts(torch_cuda, monkeypatch, T, K, N, residual, large):
     """Config-3 token counts on one GPU: y = x W^T (+ residual) against the
     fp64 product of the same bf16 values on a sample of rows that covers
-    every 256-token block's first and last rows and the ragged tail."""
+    the first and last rows of every 128-token block (so of every 256-token
+    block too) and the ragged tail."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
     monkeypatch.setenv("KRT_GEMM_LARGE_T", large)
@@ -81,7 +83,7 @@ def test_gemm_large_token_counts(torch_cuda, monkeypatch, T, K, N, residual, lar
     _lib.rowparallel_gemm_ar(None, _lib.gemm_ar_args(xd, wd, y, ws, residual=res))
     rc, bits = _lib.read_status(ws)
     assert rc == 0 and bits == 0
-    rows = sorted({t for b in range(0, T, 256) for t in (b, b + 1, min(b + 255, T - 1))} | {T - 1})
+    rows = sorted({t for b in range(0, T, 128) for t in (b, b + 1, min(b + 127, T - 1))} | {T - 1})
     idx = torch.tensor(rows, device="cuda")
     xs = xd[idx].float().cpu().numpy().astype(np.float64)
     ref = xs @ wd.float().cpu().numpy().astype(np.float64).T
