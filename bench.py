@@ -47,9 +47,12 @@ STACK_MODELS = {
 }
 L2_BYTES = 126 * 1024 * 1024
 NVLINK_GBS = 770.0  # measured B200 peer-copy bandwidth per direction over NVLink 5 (900 GB/s nominal)
-# allreduce messages (bf16 bytes) from which the NCCL route is taken: set from
-# the fused-vs-NCCL sweep (--workload gemm_ar) on B200
-NCCL_THRESHOLD = 1 << 62
+# allreduce messages (bf16 bytes) from which the NCCL route is taken, from the
+# fused-vs-NCCL config-3 sweep on two B200s (us, o_proj / down_proj): T = 64
+# fused 13.0 / 20.3 vs NCCL 29.5 / 40.8; T = 512 (4 MB) 62.4 / 99.8 vs
+# 65.8 / 93.2; T = 4096 510.7 / 802.3 vs 247.8 / 380.8.  The decode stack's
+# 1 MB messages stay on the fused exchange.
+NCCL_THRESHOLD = 8 << 20
 
 
 def peaks():
@@ -630,7 +633,9 @@ def gemm_ar_sweep(torch, comm, rank, world, tokens=GEMM_AR_TOKENS, reps=5):
     """Config 3: o_proj (K = 4096) and down_proj (K = 14336) row-parallel GEMM +
     allreduce at TP = world for each token count, through the fused exchange
     and through the NCCL route (GEMM, then ncclAllReduce), both timed on the
-    device (max over ranks) and checked against the unsharded fp32 product
+    device as 5 calls replayed from one CUDA graph (max over ranks; the weight
+    shard stays in L2 across the calls when it fits) and checked against the
+    unsharded fp32 product
     (torch on this GPU) and for bit-identity across ranks.  roofline_us =
     max(HBM bytes / HBM peak, FLOPs / bf16 peak, allreduce bus bytes / NVLink
     peak) with bus bytes 2 (N-1)/N x T x 4096 x 2 (a bf16 ring)."""
@@ -673,14 +678,22 @@ def gemm_ar_sweep(torch, comm, rank, world, tokens=GEMM_AR_TOKENS, reps=5):
                     allv = [torch.empty_like(y) for _ in range(world)]
                     dist.all_gather(allv, y)
                     same = all(torch.equal(a.view(torch.int16), allv[0].view(torch.int16)) for a in allv)
+                # device time of `reps` calls replayed from one CUDA graph (no
+                # host launch gaps; the graph is released before the next route)
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    for _ in range(reps):
+                        call()
+                gr.replay()
                 barrier(torch, world)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-                for _ in range(reps):
-                    call()
+                gr.replay()
                 e1.record()
                 barrier(torch, world)
                 us = max_over_ranks(torch, e0.elapsed_time(e1), world) * 1e3 / reps
+                torch.cuda.synchronize()
+                del gr
                 row[f"{route}_us"] = round(us, 2)
                 row[f"{route}_max_abs"] = round(float(err.max()), 4)
                 row[f"{route}_ok"] = ok and same

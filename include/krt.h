@@ -265,8 +265,11 @@ KRT_API int krt_allreduce(krt_comm* comm, const void* send, void* recv, size_t c
  * 128-feature tile, then all-gather of the bf16 result), with no separate
  * collective.  Partials travel as fp32 rounded to 15-bit mantissas and are
  * summed in fp32 in rank order, so every rank gets bit-identical results.
- * comm may be NULL for a single GPU.  Any num_tokens (launched in slices of
- * 256); k_local % 64 == 0, n_out % 128 == 0.  Calls that share a
+ * comm may be NULL for a single GPU.  Any num_tokens; k_local % 64 == 0,
+ * n_out % 128 == 0.  Up to 256 tokens one launch; more tokens run, without
+ * the fused exchange (one GPU, or the NCCL route), as one persistent GEMM
+ * over 128- or 256-token blocks that reads each weight tile once per round
+ * of CTAs, otherwise in launches of 256 tokens.  Calls that share a
  * communicator must be made in the same order, with the same shapes, on
  * every rank.
  * ---------------------------------------------------------------------- */
@@ -338,7 +341,12 @@ KRT_API int krt_paged_attention_decode(const krt_paged_attention_args* args, voi
  *
  * Both projections below normalise x first (RMSNorm with rms_weight, the
  * same cast-back order as the QKV path) and use a workspace of
- * krt_projection_workspace_size() bytes.
+ * krt_projection_workspace_size() bytes, zero-filled once before its first
+ * use.  That size includes the flags and fp32 partials of the stream-K work
+ * split (160 partial slots of 128 x num_tokens floats); a workspace of only
+ * the base size (the QKV decode workspace's) still works, without stream-K.
+ * After a call that set a timeout bit in the status word, zero the
+ * workspace again before reusing it (a stream-K flag may be left raised).
  * ---------------------------------------------------------------------- */
 KRT_API size_t krt_projection_workspace_size(int32_t num_tokens, int32_t d_model);
 

@@ -666,13 +666,42 @@ extern "C" int krt_qkv_rope_prefill(const krt_qkv_paged_args* a, void* stream) {
   p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
   p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
 
+  cudaStream_t s = (cudaStream_t)stream;
+  // The persistent projection kernel (QKV epilogue over head x 256-token
+  // tiles, issue loops without divisions) by default; KRT_PREFILL_KERNEL=0
+  // keeps the dedicated prefill kernel.
+  if (env_int("KRT_PREFILL_KERNEL", 1) != 0) {
+    PagedParams q = p;
+    q.epi = kEpiQkv;
+    q.n_pad = 256;
+    q.row_tiles = tiles;
+    const size_t budget = smem_cap_bytes() - proj_persistent_smem_bytes(0, 1, q.n_pad);
+    const size_t stage1 = 16384 + (size_t)q.n_pad * 128;
+    q.kc = (a->d_model / kBK) % 2 == 0 && budget / (2 * stage1) >= 3 ? 2 : 1;
+    q.stages = (int)(budget / (q.kc * stage1));
+    if (q.stages > 8) q.stages = 8;
+    q.tmem_cols = 512;
+    if (q.stages >= 2) {
+      CUtensorMap tmap_w, tmap_x;
+      rc = make_tmap_bf16_3d(&tmap_w, a->qkv_weight, (uint64_t)tiles * kHeadDim, (uint64_t)a->d_model,
+                             (uint64_t)a->d_model, 128, (uint32_t)q.kc);
+      if (rc) return rc;
+      rc = make_tmap_bf16_3d(&tmap_x, p.xhat, (uint64_t)a->num_tokens, (uint64_t)a->d_model, (uint64_t)a->d_model,
+                             256, (uint32_t)q.kc);
+      if (rc) return rc;
+      cudaError_t e = launch_qkv_prep(p, s);
+      if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_prefill prep launch");
+      e = launch_proj_persistent(tmap_w, tmap_x, q, tiles * ((a->num_tokens + 255) / 256), s);
+      if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_prefill launch");
+      return clear_error();
+    }
+  }
   CUtensorMap tmap_w, tmap_x;
   rc = make_tmap_bf16_2d(&tmap_w, a->qkv_weight, (uint64_t)tiles * kHeadDim, (uint64_t)a->d_model,
                          (uint64_t)a->d_model, 128);
   if (rc) return rc;
   rc = make_tmap_bf16_2d(&tmap_x, p.xhat, (uint64_t)a->num_tokens, (uint64_t)a->d_model, (uint64_t)a->d_model, 256);
   if (rc) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = launch_qkv_prep(p, s);
   if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_prefill prep launch");
   e = launch_qkv_rope_prefill(tmap_w, tmap_x, p, tiles, s);

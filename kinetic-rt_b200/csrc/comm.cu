@@ -41,6 +41,7 @@ struct krt_comm {
   bool peers_open = false;
   ncclComm_t nccl = nullptr;      // krt_comm_attach_nccl
   size_t nccl_threshold = SIZE_MAX;  // messages of at least this many bytes go through NCCL
+  float* nccl_f32 = nullptr;         // fp32 partials of the GEMM's NCCL route: [kNcclSliceTokens, max_n]
 };
 
 namespace {
@@ -382,6 +383,13 @@ extern "C" int krt_comm_attach_nccl(krt_comm* c, const void* id, size_t threshol
     if (r != ncclSuccess) return nccl_error(r, "krt_comm_attach_nccl: ncclCommInitRank");
     c->nccl = nc;
   }
+  if (!c->nccl_f32) {
+    cudaError_t e = cudaMalloc(&c->nccl_f32, (size_t)krt::kNcclSliceTokens * c->max_n * sizeof(float));
+    if (e != cudaSuccess) {
+      c->nccl_f32 = nullptr;
+      return krt::cuda_error(e, "krt_comm_attach_nccl: fp32 partial buffer");
+    }
+  }
   c->nccl_threshold = threshold_bytes;
   return clear_error();
 }
@@ -389,6 +397,7 @@ extern "C" int krt_comm_attach_nccl(krt_comm* c, const void* id, size_t threshol
 extern "C" int krt_comm_destroy(krt_comm* c) {
   if (!c) return clear_error();
   if (c->nccl && nccl_api().ok) nccl_api().comm_destroy(c->nccl);
+  if (c->nccl_f32) cudaFree(c->nccl_f32);
   for (int q = 0; q < c->world; ++q)
     if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
   if (c->local) cudaFree(c->local);
@@ -565,7 +574,8 @@ bool gemm_large_t_eligible(const krt_gemm_ar_args* a) {
   return 2 * tiles >= device_sm_count();
 }
 
-int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, int* status, cudaStream_t s) {
+// y32 != nullptr: fp32 [T, n_out] out instead of bf16 y (no residual).
+int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, float* y32, int* status, cudaStream_t s) {
   PagedParams q;
   std::memset(&q, 0, sizeof(q));
   q.num_tokens = a->num_tokens;
@@ -574,8 +584,9 @@ int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, int* status, c
   q.status = status;
   q.epi = kEpiStore;
   q.y = static_cast<__nv_bfloat16*>(a->y);
-  q.y_stride = a->y_stride;
-  q.residual = static_cast<const __nv_bfloat16*>(residual);
+  q.y_stride = y32 ? a->n_out : a->y_stride;
+  q.y32 = y32;
+  q.residual = y32 ? nullptr : static_cast<const __nv_bfloat16*>(residual);
   q.row_tiles = a->n_out / 128;
   const size_t cap = (size_t)env_int_value("KRT_SMEM_CAP_KB", 227) * 1024;
   const size_t budget = cap - proj_persistent_smem_bytes(0, 1, q.n_pad);
@@ -598,6 +609,117 @@ int gemm_large_t(const krt_gemm_ar_args* a, const void* residual, int* status, c
   return KRT_OK;
 }
 
+// One launch per 256 tokens of the decode-shaped GEMM (+ exchange when
+// p.comm.world > 1).  Every slice's parameters and tensor maps are built
+// before the first launch: with a communicator, every rank must make the same
+// launches (the exchange epochs count them), so a call that fails on the host
+// fails before any of its kernels run.  y32 != nullptr: fp32 [T, n_out] out
+// (world 1, no residual).
+struct GemmSlice {
+  GemmArParams p;
+  GemmCfg cfg;
+  CUtensorMap tmap_w, tmap_x;
+};
+int build_gemm_slices(const krt_gemm_ar_args* a, const void* residual, float* y32, const GemmArParams& base,
+                      std::vector<GemmSlice>& slices) {
+  const int num_kb = a->k_local / 64;
+  slices.reserve((size_t)(a->num_tokens + 255) / 256);
+  for (int t0 = 0; t0 < a->num_tokens; t0 += 256) {
+    const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
+    GemmSlice sl;
+    sl.p = base;
+    sl.p.num_tokens = T;
+    sl.p.n_pad = (T + 15) / 16 * 16;
+    sl.cfg = gemm_config(a->n_out, num_kb, sl.p.n_pad, base.comm.world);
+    sl.p.kc = sl.cfg.kc;
+    sl.p.stages = sl.cfg.stages;
+    sl.p.splits = sl.cfg.splits;
+    // L2 prefetch of weight stages ahead of the ring: off by default (it
+    // shortens o_proj alone, 10.7 -> 10.3 us, but lengthens the chained
+    // decoder-layer step); KRT_L2_PREFETCH_STAGES turns it on.
+    sl.p.prefetch = env_int_value("KRT_L2_PREFETCH_STAGES", 0);
+    int cols = 32;
+    while (cols < sl.p.n_pad) cols <<= 1;
+    sl.p.tmem_cols = cols;
+    sl.p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
+    sl.p.y32 = y32 ? y32 + (size_t)t0 * a->n_out : nullptr;
+    sl.p.residual = residual && !y32 ? static_cast<const __nv_bfloat16*>(residual) + (size_t)t0 * a->y_stride
+                                     : nullptr;
+    const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
+    int rc = make_tmap_bf16_3d(&sl.tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local,
+                               (uint64_t)a->k_local, (uint32_t)sl.cfg.tile_m, (uint32_t)sl.p.kc);
+    if (rc) return rc;
+    rc = make_tmap_bf16_3d(&sl.tmap_x, xp, (uint64_t)T, (uint64_t)a->k_local, (uint64_t)a->x_stride,
+                           (uint32_t)sl.p.n_pad, (uint32_t)sl.p.kc);
+    if (rc) return rc;
+    slices.push_back(sl);
+  }
+  return KRT_OK;
+}
+
+// This GPU's product alone, any token count: bf16 y (+ residual), or fp32
+// y32 [T, n_out] (no residual).
+int gemm_local(const krt_gemm_ar_args* a, const void* residual, float* y32, int* status, cudaStream_t s) {
+  if (gemm_large_t_eligible(a)) return gemm_large_t(a, residual, y32, status, s);
+  GemmArParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.comm.world = 1;
+  p.comm.rank = 0;
+  p.n_out = a->n_out;
+  p.k_local = a->k_local;
+  p.y_stride = a->y_stride;
+  p.status = status;
+  std::vector<GemmSlice> slices;
+  int rc = build_gemm_slices(a, residual, y32, p, slices);
+  if (rc) return rc;
+  for (const GemmSlice& sl : slices) {
+    cudaError_t e = launch_rowparallel_gemm_ar(sl.cfg.tile_m, sl.tmap_w, sl.tmap_x, sl.p, sl.cfg.tiles, s);
+    if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
+  }
+  return KRT_OK;
+}
+
+// y[t, n] = bf16(y32[t, n] + residual[t, n]): the NCCL route's single
+// rounding, eight features per thread (16-byte loads and stores).
+__global__ void __launch_bounds__(256) nccl_finish_kernel(const float* __restrict__ y32,
+                                                          const __nv_bfloat16* __restrict__ residual,
+                                                          __nv_bfloat16* __restrict__ y, int T, int n_out,
+                                                          int y_stride) {
+  const long long groups = (long long)T * (n_out / 8);
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < groups;
+       g += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(g / (n_out / 8));
+    const int n = (int)(g % (n_out / 8)) * 8;
+    const float4* src = reinterpret_cast<const float4*>(y32 + (size_t)t * n_out + n);
+    float v[8];
+    const float4 a0 = src[0], a1 = src[1];
+    v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+    v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+    if (residual) {
+      const uint4 r = *reinterpret_cast<const uint4*>(residual + (size_t)t * y_stride + n);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(b2[q]);
+        v[2 * q] += f.x;
+        v[2 * q + 1] += f.y;
+      }
+    }
+    *reinterpret_cast<uint4*>(y + (size_t)t * y_stride + n) =
+        make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
+}
+
+cudaError_t launch_nccl_finish(const float* y32, const __nv_bfloat16* residual, __nv_bfloat16* y, int T, int n_out,
+                               int y_stride, cudaStream_t s) {
+  const long long groups = (long long)T * (n_out / 8);
+  long long blocks = (groups + 255) / 256;
+  const long long cap = 4LL * device_sm_count();
+  if (blocks > cap) blocks = cap;
+  nccl_finish_kernel<<<(unsigned)blocks, 256, 0, s>>>(y32, residual, y, T, n_out, y_stride);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 extern "C" size_t krt_rowparallel_gemm_ar_workspace_size(void) { return kWsHeaderBytes; }
@@ -617,91 +739,62 @@ extern "C" int krt_rowparallel_gemm_ar(krt_comm* c, const krt_gemm_ar_args* a, v
   if (!a->workspace || a->workspace_bytes < kWsHeaderBytes)
     return set_error(KRT_ERR_WORKSPACE, "krt_rowparallel_gemm_ar: workspace of %zu bytes, %zu needed",
                      a->workspace_bytes, (size_t)kWsHeaderBytes);
-  GemmArParams p;
-  std::memset(&p, 0, sizeof(p));
-  // Large outputs with an NCCL communicator attached: the GEMM runs without
-  // the fused exchange (its partial lands in y, comm rank 0 adding the
-  // residual, so the sum holds it once) and one in-place ncclAllReduce of y
-  // follows.  Every rank takes the same route (same sizes, same threshold).
-  const bool via_nccl = c && c->world > 1 && c->nccl && a->y_stride == a->n_out &&
-                        (size_t)a->num_tokens * a->n_out * 2 >= c->nccl_threshold;
-  if (c && !via_nccl) {
-    int rc = comm_view(c, &p.comm);
-    if (rc) return rc;
-    if (a->n_out > c->max_n)
-      return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: n_out %d exceeds the communicator's %d",
-                       a->n_out, c->max_n);
-  } else {
-    p.comm.world = 1;
-    p.comm.rank = 0;
-  }
-  const void* residual = via_nccl && c->rank != 0 ? nullptr : a->residual;
-  const int num_kb = a->k_local / 64;
-  p.n_out = a->n_out;
-  p.k_local = a->k_local;
-  p.y_stride = a->y_stride;
-  p.status = static_cast<int*>(a->workspace);
   if (a->residual && (reinterpret_cast<uintptr_t>(a->residual) & 15))
     return set_error(KRT_ERR_INVALID, "krt_rowparallel_gemm_ar: residual must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
-  if (p.comm.world == 1 && gemm_large_t_eligible(a)) {
-    int rc = gemm_large_t(a, residual, p.status, s);
-    if (rc) return rc;
-    if (via_nccl) {
-      ncclResult_t r = nccl_api().all_reduce(a->y, a->y, (size_t)a->num_tokens * a->n_out, ncclBfloat16, ncclSum,
-                                             c->nccl, s);
+  int* status = static_cast<int*>(a->workspace);
+  // Large outputs with an NCCL communicator attached: per slice of up to
+  // kNcclSliceTokens tokens the GEMM writes this rank's fp32 partial into the
+  // communicator's buffer, one ncclAllReduce sums the partials in fp32, and
+  // nccl_finish_kernel adds the residual and rounds to bf16 once (bf16
+  // partials can miss the bf16 tolerance where partials cancel).  Every rank
+  // takes the same route (same sizes, same threshold).
+  const bool via_nccl = c && c->world > 1 && c->nccl && c->nccl_f32 &&
+                        (size_t)a->num_tokens * a->n_out * 2 >= c->nccl_threshold;
+  if (via_nccl) {
+    if (a->n_out > c->max_n)
+      return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: n_out %d exceeds the communicator's %d",
+                       a->n_out, c->max_n);
+    for (int t0 = 0; t0 < a->num_tokens; t0 += kNcclSliceTokens) {
+      krt_gemm_ar_args sub = *a;
+      sub.num_tokens = a->num_tokens - t0 < kNcclSliceTokens ? a->num_tokens - t0 : kNcclSliceTokens;
+      sub.x = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
+      sub.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
+      sub.residual = a->residual ? static_cast<const __nv_bfloat16*>(a->residual) + (size_t)t0 * a->y_stride
+                                 : nullptr;
+      int rc = gemm_local(&sub, nullptr, c->nccl_f32, status, s);
+      if (rc) return rc;
+      const size_t count = (size_t)sub.num_tokens * a->n_out;
+      ncclResult_t r = nccl_api().all_reduce(c->nccl_f32, c->nccl_f32, count, ncclFloat32, ncclSum, c->nccl, s);
       if (r != ncclSuccess) return nccl_error(r, "krt_rowparallel_gemm_ar: ncclAllReduce");
+      cudaError_t e = launch_nccl_finish(c->nccl_f32, static_cast<const __nv_bfloat16*>(sub.residual),
+                                         static_cast<__nv_bfloat16*>(sub.y), sub.num_tokens, a->n_out, a->y_stride, s);
+      if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar: finish launch");
     }
     return clear_error();
   }
-  // Every slice's parameters and tensor maps are built before the first
-  // launch: with a communicator, every rank must make the same launches (the
-  // exchange epochs count them), so a call that fails on the host fails
-  // before any of its kernels run.
-  struct Slice {
-    GemmArParams p;
-    GemmCfg cfg;
-    CUtensorMap tmap_w, tmap_x;
-  };
-  std::vector<Slice> slices;
-  slices.reserve((size_t)(a->num_tokens + 255) / 256);
-  for (int t0 = 0; t0 < a->num_tokens; t0 += 256) {
-    const int T = (a->num_tokens - t0) < 256 ? (a->num_tokens - t0) : 256;
-    Slice sl;
-    sl.p = p;
-    sl.p.num_tokens = T;
-    sl.p.n_pad = (T + 15) / 16 * 16;
-    sl.cfg = gemm_config(a->n_out, num_kb, sl.p.n_pad, p.comm.world);
-    sl.p.kc = sl.cfg.kc;
-    sl.p.stages = sl.cfg.stages;
-    sl.p.splits = sl.cfg.splits;
-    // L2 prefetch of weight stages ahead of the ring: off by default (it
-    // shortens o_proj alone, 10.7 -> 10.3 us, but lengthens the chained
-    // decoder-layer step); KRT_L2_PREFETCH_STAGES turns it on.
-    sl.p.prefetch = env_int_value("KRT_L2_PREFETCH_STAGES", 0);
-    int cols = 32;
-    while (cols < sl.p.n_pad) cols <<= 1;
-    sl.p.tmem_cols = cols;
-    sl.p.y = static_cast<__nv_bfloat16*>(a->y) + (size_t)t0 * a->y_stride;
-    sl.p.residual =
-        residual ? static_cast<const __nv_bfloat16*>(residual) + (size_t)t0 * a->y_stride : nullptr;
-    const void* xp = static_cast<const __nv_bfloat16*>(a->x) + (size_t)t0 * a->x_stride;
-    int rc = make_tmap_bf16_3d(&sl.tmap_w, a->weight, (uint64_t)a->n_out, (uint64_t)a->k_local,
-                               (uint64_t)a->k_local, (uint32_t)sl.cfg.tile_m, (uint32_t)sl.p.kc);
-    if (rc) return rc;
-    rc = make_tmap_bf16_3d(&sl.tmap_x, xp, (uint64_t)T, (uint64_t)a->k_local, (uint64_t)a->x_stride,
-                           (uint32_t)sl.p.n_pad, (uint32_t)sl.p.kc);
-    if (rc) return rc;
-    slices.push_back(sl);
+  if (!c || c->world == 1) {
+    int rc = gemm_local(a, a->residual, nullptr, status, s);
+    return rc ? rc : clear_error();
   }
-  for (const Slice& sl : slices) {
+  // The fused exchange, in launches of up to 256 tokens.
+  GemmArParams p;
+  std::memset(&p, 0, sizeof(p));
+  int rc = comm_view(c, &p.comm);
+  if (rc) return rc;
+  if (a->n_out > c->max_n)
+    return set_error(KRT_ERR_UNSUPPORTED, "krt_rowparallel_gemm_ar: n_out %d exceeds the communicator's %d",
+                     a->n_out, c->max_n);
+  p.n_out = a->n_out;
+  p.k_local = a->k_local;
+  p.y_stride = a->y_stride;
+  p.status = status;
+  std::vector<GemmSlice> slices;
+  rc = build_gemm_slices(a, a->residual, nullptr, p, slices);
+  if (rc) return rc;
+  for (const GemmSlice& sl : slices) {
     cudaError_t e = launch_rowparallel_gemm_ar(sl.cfg.tile_m, sl.tmap_w, sl.tmap_x, sl.p, sl.cfg.tiles, s);
     if (e != cudaSuccess) return cuda_error(e, "krt_rowparallel_gemm_ar launch");
-  }
-  if (via_nccl) {
-    ncclResult_t r = nccl_api().all_reduce(a->y, a->y, (size_t)a->num_tokens * a->n_out, ncclBfloat16, ncclSum,
-                                           c->nccl, s);
-    if (r != ncclSuccess) return nccl_error(r, "krt_rowparallel_gemm_ar: ncclAllReduce");
   }
   return clear_error();
 }

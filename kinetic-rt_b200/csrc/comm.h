@@ -94,8 +94,13 @@ struct CommView {
 };
 
 // Launch parameters of the fused row-parallel GEMM + allreduce (gemm_ar.cu).
+// Tokens per NCCL-route slice: the communicator's fp32 partial buffer holds
+// kNcclSliceTokens x max_n floats.
+constexpr int kNcclSliceTokens = 4096;
+
 struct GemmArParams {
   __nv_bfloat16* y;
+  float* y32;  // world 1 only: fp32 out [num_tokens, n_out] instead of y (no residual)
   const __nv_bfloat16* residual;  // optional: y = residual + sum (same strides as y; may be y itself)
   int y_stride;
   int num_tokens, n_pad, n_out, k_local;

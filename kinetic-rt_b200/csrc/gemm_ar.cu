@@ -404,7 +404,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (world == 1) {
-        if (alive && t < T) {
+        if (alive && t < T && p.y32) {
+          float4* dst = reinterpret_cast<float4*>(p.y32 + (size_t)t * p.n_out + row0 + RG * g);
+#pragma unroll
+          for (int k4 = 0; k4 < RG / 4; ++k4) dst[k4] = make_float4(y[4 * k4], y[4 * k4 + 1], y[4 * k4 + 2], y[4 * k4 + 3]);
+        } else if (alive && t < T) {
           add_residual_rows<RG>(y, p.residual ? p.residual + (size_t)t * p.y_stride + row0 + RG * g : nullptr);
           uint32_t w[RG / 2];
 #pragma unroll

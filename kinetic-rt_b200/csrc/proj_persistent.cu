@@ -46,9 +46,11 @@
 // up rows side by side in 64-row groups), kEpiArgmax (the CTA keeps each
 // token's best (logit, index) over all its tiles in shared memory and folds
 // it into the global keys once at the end; one token block) and kEpiStore
-// (y = bf16(acc + residual): the row-parallel GEMM at large token counts).  The kEpiQkv branch (bias, RoPE,
-// Q out, K/V into the pool) mirrors the prefill kernel's epilogue; the
-// launcher does not offer it (QKV runs on the split-K decode kernel).
+// (y = bf16(acc + residual): the row-parallel GEMM at large token counts).
+// kEpiQkv (bias, RoPE, Q out, K/V into the paged pool; tile = one head x
+// one token block) serves the QKV prefill: every tile stages its block's
+// positions and pool slots in shared memory once the previous tile's
+// epilogue is done with them.  (Decode-sized QKV runs on the split-K kernel.)
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -269,11 +271,12 @@ __global__ void __launch_bounds__(kPjThreads, 1)
       }
       const uint32_t buf = (uint32_t)local & 1u;
       const uint32_t use = (uint32_t)local >> 1;
-      if (EPI == kEpiQkv && local == 0) {
-        // token metadata once (the same batch for every tile)
+      const int qh = tile % RT;  // kEpiQkv: the head (weight row tile)
+      if (EPI == kEpiQkv) {
+        // this tile's token metadata (the previous tile's epilogue is done with it)
         for (int t = ept; t < n_pad; t += 256) {
-          tl->pos[t] = t < T ? p.tok_pos[t] : -1;
-          tl->slot[t] = t < T ? p.tok_slot[t] : -1;
+          tl->pos[t] = t < T ? p.tok_pos[t_base + t] : -1;
+          tl->slot[t] = t < T ? p.tok_slot[t_base + t] : -1;
         }
       }
       const bool waited = mbar_wait_warp(&tl->tmem_full[buf], use & 1u, abort_flag);
@@ -304,8 +307,8 @@ __global__ void __launch_bounds__(kPjThreads, 1)
         if (lane == 0) mbar_arrive(&tl->tmem_empty[buf]);
         continue;
       }
-      const float bias_r = EPI == kEpiQkv && p.bias ? __bfloat162float(p.bias[tile * kHeadDim + r]) : 0.f;
-      const bool rot = EPI == kEpiQkv ? tile < p.n_heads + p.n_kv_heads : (EPI == kEpiSwiglu ? g8 < 4 : false);
+      const float bias_r = EPI == kEpiQkv && p.bias ? __bfloat162float(p.bias[qh * kHeadDim + r]) : 0.f;
+      const bool rot = EPI == kEpiQkv ? qh < p.n_heads + p.n_kv_heads : (EPI == kEpiSwiglu ? g8 < 4 : false);
       for (int c0 = grp * 16; c0 < n_pad; c0 += 32) {
         if (c0 >= T) break;  // uniform within the group
         const int t = c0 + j;
@@ -327,7 +330,11 @@ __global__ void __launch_bounds__(kPjThreads, 1)
           ld_smem_16f(ybuf + j * kYStride + 16 * g8, y);
           if (rot) ld_smem_16f(ybuf + j * kYStride + 16 * (g8 ^ 4), yp);
           if (EPI == kEpiQkv) {
-            store_rows_n<16>(p, tile, t, 16 * g8, g8 < 4 ? -1.f : 1.f, pos, tl->slot[t], y, yp, cs, sn);
+            store_rows_n<16>(p, qh, t_base + t, 16 * g8, g8 < 4 ? -1.f : 1.f, pos, tl->slot[t], y, yp, cs, sn);
+          } else if (EPI == kEpiStore && p.y32) {
+            float4* dst = reinterpret_cast<float4*>(p.y32 + (size_t)(t_base + t) * p.y_stride + w_row(tile) + 16 * g8);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
           } else if (EPI == kEpiStore) {
             const size_t off = (size_t)(t_base + t) * p.y_stride + w_row(tile) + 16 * g8;
             if (p.residual) {
@@ -433,7 +440,8 @@ cudaError_t launch_proj_persistent(const CUtensorMap& tmap_w, const CUtensorMap&
   if (p.epi == kEpiSwiglu) return launch_pj_t<kEpiSwiglu>(tmap_w, tmap_x, p, num_tiles, stream);
   if (p.epi == kEpiArgmax) return launch_pj_t<kEpiArgmax>(tmap_w, tmap_x, p, num_tiles, stream);
   if (p.epi == kEpiStore) return launch_pj_t<kEpiStore>(tmap_w, tmap_x, p, num_tiles, stream);
-  return cudaErrorInvalidValue;  // the QKV projection runs on the split-K decode kernel
+  if (p.epi == kEpiQkv) return launch_pj_t<kEpiQkv>(tmap_w, tmap_x, p, num_tiles, stream);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace krt

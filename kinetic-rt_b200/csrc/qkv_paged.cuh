@@ -64,6 +64,7 @@ struct PagedParams {
   __nv_bfloat16* y;     // kEpiStore: [num_tokens, y_stride] bf16(acc + residual)
   int y_stride;
   const __nv_bfloat16* residual;  // kEpiStore: optional, same layout as y
+  float* y32;           // kEpiStore: fp32 out (row stride y_stride, no residual) instead of y
 };
 
 // Epilogues of the decode-shaped (swap-AB, split-K) projection kernel:

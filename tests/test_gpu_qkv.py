@@ -134,6 +134,15 @@ def test_paged_llama_shapes(torch_cuda, krt, kind, num_seqs, tokens_per_seq, ctx
         assert torch.equal(q1, d["q"])
 
 
+@pytest.mark.parametrize("num_seqs,tokens_per_seq", [(1, 300), (3, 100)])
+def test_prefill_dedicated_kernel(torch_cuda, krt, monkeypatch, num_seqs, tokens_per_seq):
+    """KRT_PREFILL_KERNEL=0: the dedicated prefill kernel instead of the
+    persistent projection kernel's QKV epilogue; the same oracle checks."""
+    monkeypatch.setenv("KRT_PREFILL_KERNEL", "0")
+    test_paged_llama_shapes(torch_cuda, krt, "prefill", num_seqs, tokens_per_seq, None)
+    test_paged_gqa_golden(torch_cuda, krt, "prefill")
+
+
 def test_prefill_full_size_sampled(torch_cuda, krt):
     """8 sequences x 2048 tokens (the full prefill configuration): sampled
     rows against the oracle, every token's K/V placement bit-exact."""
