@@ -322,7 +322,9 @@ DecodeCfg decode_config(int heads, int num_kb, int n_pad, bool whole_tiles = fal
   // splits fill about two thirds of the SMs: more CTAs exchange more partials
   // than their extra streaming gains (B200, 64 tokens: 24 half-head tiles
   // x 4 splits 10.1 us, x 6 splits 10.6 us)
-  int s = forced > 0 ? forced : device_sm_count() * 2 / 3 / tiles;
+  // (projections on whole tiles, gate/up at TP=8: 28 tiles x 4 splits 16.7 us,
+  // x 3 splits 19.4 us, x 5 splits 26.4 us: about four fifths of the SMs)
+  int s = forced > 0 ? forced : device_sm_count() * (whole_tiles ? 4 : 2) / (whole_tiles ? 5 : 3) / tiles;
   if (s > 8) s = 8;
   if (s < 1) s = 1;
   for (; s >= 1; --s) {
@@ -416,6 +418,7 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   p.tok_slot = reinterpret_cast<long long*>(ws + L.slot_off);
   p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
 
+  cudaStream_t s = (cudaStream_t)stream;
   CUtensorMap tmap_w, tmap_x;
   if (cfg.tile_m == 64)
     rc = make_tmap_bf16_half_heads(&tmap_w, a->qkv_weight, tiles, (uint64_t)a->d_model, (uint32_t)p.kc);
@@ -426,7 +429,6 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   rc = make_tmap_bf16_3d(&tmap_x, p.xhat, (uint64_t)p.num_tokens, (uint64_t)a->d_model, (uint64_t)a->d_model,
                          (uint32_t)p.n_pad, (uint32_t)p.kc);
   if (rc) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = launch_qkv_prep(p, s);
   if (e != cudaSuccess) return cuda_error(e, "krt_qkv_rope_decode prep launch");
   e = launch_qkv_rope_decode(cfg.tile_m, tmap_w, tmap_x, p, cfg.tiles, s);
@@ -667,10 +669,10 @@ extern "C" int krt_qkv_rope_prefill(const krt_qkv_paged_args* a, void* stream) {
   p.xhat = reinterpret_cast<__nv_bfloat16*>(ws + L.xhat_off);
 
   cudaStream_t s = (cudaStream_t)stream;
-  // The persistent projection kernel (QKV epilogue over head x 256-token
-  // tiles, issue loops without divisions) by default; KRT_PREFILL_KERNEL=0
-  // keeps the dedicated prefill kernel.
-  if (env_int("KRT_PREFILL_KERNEL", 1) != 0) {
+  // KRT_PREFILL_KERNEL=1: the persistent projection kernel's QKV epilogue
+  // over head x 256-token tiles instead of the dedicated prefill kernel (the
+  // same speed on B200 at 8 x 2048 tokens: 1112 vs 1115 TFLOP/s).
+  if (env_int("KRT_PREFILL_KERNEL", 0) == 1) {
     PagedParams q = p;
     q.epi = kEpiQkv;
     q.n_pad = 256;

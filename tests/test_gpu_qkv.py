@@ -135,10 +135,10 @@ def test_paged_llama_shapes(torch_cuda, krt, kind, num_seqs, tokens_per_seq, ctx
 
 
 @pytest.mark.parametrize("num_seqs,tokens_per_seq", [(1, 300), (3, 100)])
-def test_prefill_dedicated_kernel(torch_cuda, krt, monkeypatch, num_seqs, tokens_per_seq):
-    """KRT_PREFILL_KERNEL=0: the dedicated prefill kernel instead of the
-    persistent projection kernel's QKV epilogue; the same oracle checks."""
-    monkeypatch.setenv("KRT_PREFILL_KERNEL", "0")
+def test_prefill_persistent_kernel(torch_cuda, krt, monkeypatch, num_seqs, tokens_per_seq):
+    """KRT_PREFILL_KERNEL=1: the persistent projection kernel's QKV epilogue
+    instead of the dedicated prefill kernel; the same oracle checks."""
+    monkeypatch.setenv("KRT_PREFILL_KERNEL", "1")
     test_paged_llama_shapes(torch_cuda, krt, "prefill", num_seqs, tokens_per_seq, None)
     test_paged_gqa_golden(torch_cuda, krt, "prefill")
 
