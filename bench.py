@@ -923,6 +923,15 @@ def run_stack(args, rank, world, local_rank):
     dec.check_status()
     prefill = prefill_entry(torch, rank, world) if model == "8b" else None
     del graph
+    # whole-model prompt prefill: config 5's 4 x 8192 on the 70b stack; 8 x 2048
+    # (config 2's prompts) on the 8b stack at N = 1
+    prompt = None
+    pf_seqs, pf_len = (4, 8192) if model == "70b" else (8, 2048)
+    if model == "70b" or world == 1:
+        try:
+            prompt = prompt_prefill(torch, shape, weights, comm, rank, world, pf_seqs, pf_len)
+        except Exception as exc:  # reported in the line; the decode numbers stand
+            prompt = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     base = None
     if world == 1 and model == "8b":
         base = cpu_stack_sample()
@@ -946,6 +955,7 @@ def run_stack(args, rank, world, local_rank):
                      "achieved_GBps": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
                      "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4), "context_mid": ctx_mid},
             "kernels": klist + ([prefill] if prefill else []),
+            "prompt_prefill": prompt,
             "parity": parity,
             "config3_gemm_ar": config3,
             "cpu_baseline": base if base else {"value": None, "note": "timed at N=1 on the 8b stack only (rank 0 "
@@ -965,6 +975,51 @@ def run_stack(args, rank, world, local_rank):
     if bad:
         print("parity check failed", file=sys.stderr)
         sys.exit(3)
+
+
+def prompt_prefill(torch, shape, weights, comm, rank, world, seqs, prompt_len):
+    """A whole-model prefill: `seqs` random prompts of `prompt_len` tokens
+    through PagedDecoder.prefill (prefill QKV, causal prefill attention,
+    GEMM + allreduce and gate/up over whole prompts, lm_head + greedy on the
+    last tokens), timed on the device (max over ranks) after a short untimed
+    prefill of the same decoder.  FLOPs: 2 x tokens x (per-layer weights + the
+    lm_head on the last tokens only) plus the causal attention, this rank's
+    share."""
+    from python.kinetic_rt.decoder import PagedDecoder
+    dec = PagedDecoder(torch, shape, weights, seqs, prompt_len + 16, comm, rank, world)
+    g = torch.Generator().manual_seed(13)
+    warm = [torch.randint(0, shape.vocab, (min(prompt_len, 256),), generator=g) for _ in range(seqs)]
+    prompts = [torch.randint(0, shape.vocab, (prompt_len,), generator=g) for _ in range(seqs)]
+    dec.prefill(warm, group=seqs)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    tok = dec.prefill(prompts, group=seqs)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    ms = max_over_ranks(torch, e0.elapsed_time(e1), world)
+    dec.check_status()
+    same = True
+    if world > 1:
+        import torch.distributed as dist
+        toks = [torch.empty_like(tok) for _ in range(world)]
+        dist.all_gather(toks, tok)
+        same = all(torch.equal(t, toks[0]) for t in toks)
+    D, hd = shape.d_model, shape.head_dim
+    layer_params = ((shape.n_heads + 2 * shape.n_kv_heads) * hd * D + D * shape.n_heads * hd + 3 * D * shape.inter)
+    T = seqs * prompt_len
+    flops = (2.0 * T * layer_params * shape.n_layers + 2.0 * seqs * shape.vocab * D
+             + shape.n_layers * seqs * shape.n_heads * hd * 4.0 * prompt_len * (prompt_len + 1) / 2) / world
+    del dec
+    torch.cuda.empty_cache()
+    return {"seqs": seqs, "prompt_tokens": prompt_len, "ms": round(ms, 2), "tokens_per_s": round(T / (ms * 1e-3), 1),
+            "flops_per_gpu": int(flops), "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12, 1),
+            "first_tokens_identical_across_ranks": same,
+            "how": "PagedDecoder.prefill: per layer prefill QKV + causal prefill attention + o_proj GEMM+allreduce "
+                   "+ gate/up + down_proj GEMM+allreduce over whole prompts, then lm_head + greedy on the last "
+                   "tokens; one run, device time, max over ranks"}
 
 
 def _lm(dec):

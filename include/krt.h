@@ -329,6 +329,38 @@ KRT_API size_t krt_paged_attention_workspace_size(int32_t num_seqs, int32_t n_he
                                                   int32_t max_seq_len);
 KRT_API int krt_paged_attention_decode(const krt_paged_attention_args* args, void* stream);
 
+/* Causal paged attention for prompt tokens (prefill), GQA, bf16.  No
+ * reference counterpart either (its generate loop recomputes the whole
+ * sequence per token, python/kinetic_rt/orchestrator.py:419-448); it reads the
+ * pool the prefill QKV kernel (krt_qkv_rope_prefill) scattered K/V into.
+ * Sequence s has q_len = q_start[s + 1] - q_start[s] query tokens, rows
+ * q_start[s] .. of q and out, at positions q_pos0[s] .. q_pos0[s] + q_len - 1;
+ * the query at position p attends to the sequence's pool tokens 0 .. p (with
+ * q_pos0 > 0 after a prefix already in the pool).  out[t, h] =
+ * softmax(q[t, h] . K^T * scale) V over those tokens, kvh(h) = h / (n_heads /
+ * n_kv_heads); n_heads / n_kv_heads must divide 16.  The workspace holds the
+ * status word (krt_read_status): bit 8 for a block-table entry out of range
+ * (that chunk is masked) or a q_len above max_q_len (rows past it are not
+ * written), timeouts as elsewhere. */
+typedef struct krt_paged_prefill_attention_args {
+  const void* q;       /* bf16 [T, q_stride], query head h at columns h * 128 */
+  void* out;           /* bf16 [T, out_stride] */
+  const void* kv_pool; /* this layer's pool, [block][token][K|V][kv_head][128] bf16 */
+  const int32_t* block_table; /* [num_seqs, block_table_stride] */
+  const int32_t* q_start;     /* [num_seqs + 1] first query row of each sequence, then T */
+  const int32_t* q_pos0;      /* [num_seqs] position of each sequence's first query token */
+  int32_t num_seqs, n_heads, n_kv_heads, head_dim;
+  int32_t q_stride, out_stride;
+  int32_t block_table_stride, num_blocks, tokens_per_block;
+  int32_t max_q_len;   /* upper bound of q_len over the sequences: sizes the grid */
+  float scale;         /* softmax scale; 0 = 1 / sqrt(head_dim) */
+  void* workspace;
+  size_t workspace_bytes;
+} krt_paged_prefill_attention_args;
+
+KRT_API size_t krt_paged_attention_prefill_workspace_size(void);
+KRT_API int krt_paged_attention_prefill(const krt_paged_prefill_attention_args* args, void* stream);
+
 /* -------------------------------------------------------------------------
  * The rest of a decode step (batch of up to 256 tokens, bf16, fp32
  * accumulation).  The reference has no decoder forward; these are the
@@ -354,7 +386,9 @@ KRT_API size_t krt_projection_workspace_size(int32_t num_tokens, int32_t d_model
  * intermediate features (this rank's inter_local of them).  The weight keeps
  * gate and up rows side by side in 64-row groups: rows 128 i .. 128 i + 63
  * are gate rows of features 64 i .. 64 i + 63 and the next 64 rows are the up
- * rows of the same features (a load-time interleave of the two shards). */
+ * rows of the same features (a load-time interleave of the two shards).
+ * num_tokens up to 256 for a decode step, or a whole prompt (up to 2^20
+ * tokens: the persistent kernel over 256-token blocks). */
 typedef struct krt_gate_up_args {
   const void* x;              /* bf16 [num_tokens, d_model], row stride x_stride */
   const void* rms_weight;     /* bf16 [d_model] */

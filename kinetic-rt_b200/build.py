@@ -31,7 +31,7 @@ CUDA_INC = "/usr/local/cuda/include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 EXT = sysconfig.get_config_var("EXT_SUFFIX")
 
-LIB_SOURCES = ["capi.cu", "qkv_generic.cu", "qkv_prep.cu", "qkv_decode.cu", "qkv_decode_noalloc.cu", "qkv_prefill.cu", "gemm_ar.cu", "comm.cu", "attn_decode.cu", "proj_persistent.cu"]
+LIB_SOURCES = ["capi.cu", "qkv_generic.cu", "qkv_prep.cu", "qkv_decode.cu", "qkv_decode_noalloc.cu", "qkv_prefill.cu", "gemm_ar.cu", "comm.cu", "attn_decode.cu", "attn_prefill.cu", "proj_persistent.cu"]
 
 
 def _pybind_includes():

@@ -477,7 +477,17 @@ int run_projection(PagedParams& p, const void* weight, int weight_rows, const ch
   // per SM walking the tiles with the weight stream never drained; stream-K
   // below 0.6 tiles per SM and between one and three, whole tiles otherwise.
   // KRT_PROJ_PERSISTENT=0 / 1 and KRT_PROJ_STREAMK=0 / 1 force either choice.
-  const int forced = env_int("KRT_PROJ_PERSISTENT", -1);
+  // More than 256 tokens (a prompt): the persistent kernel over 256-token
+  // blocks, whole tiles.
+  const bool blocks = p.num_tokens > 256;
+  if (blocks) {
+    p.n_pad = 256;
+    p.row_tiles = tiles;
+    p.sk_part = nullptr;
+    p.sk_flags = nullptr;
+  }
+  const int n_blocks = (p.num_tokens + 255) / 256;
+  const int forced = blocks ? 1 : env_int("KRT_PROJ_PERSISTENT", -1);
   const int sk_forced = env_int("KRT_PROJ_STREAMK", -1);
   const bool sk_possible = p.sk_part != nullptr && sk_forced != 0;  // the workspace holds the partials
   const bool sk_auto = 10 * tiles < 6 * sms || (tiles >= sms && tiles < 3 * sms);
@@ -505,10 +515,11 @@ int run_projection(PagedParams& p, const void* weight, int weight_rows, const ch
       if (rc) return rc;
       cudaError_t e = launch_qkv_prep(p, s);
       if (e != cudaSuccess) return cuda_error(e, name);
-      e = launch_proj_persistent(tmap_w, tmap_x, p, tiles, s);
+      e = launch_proj_persistent(tmap_w, tmap_x, p, tiles * n_blocks, s);
       if (e != cudaSuccess) return cuda_error(e, name);
       return clear_error();
     }
+    if (blocks) return set_error(KRT_ERR_UNSUPPORTED, "%s: shared memory too small for 256-token blocks", name);
   }
   const DecodeCfg cfg = decode_config(tiles, num_kb, p.n_pad, true);
   p.kc = cfg.kc;
@@ -534,10 +545,11 @@ int run_projection(PagedParams& p, const void* weight, int weight_rows, const ch
 
 // Shared checks and parameters of the RMSNorm + projection calls.
 int projection_params(PagedParams& p, const char* name, const void* x, const void* gamma, const void* weight,
-                      int num_tokens, int d_model, int x_stride, float eps, void* workspace, size_t ws_bytes) {
+                      int num_tokens, int d_model, int x_stride, float eps, void* workspace, size_t ws_bytes,
+                      int max_tokens = 256) {
   if (!x || !gamma || !weight || !workspace) return set_error(KRT_ERR_INVALID, "%s: a required pointer is NULL", name);
-  if (num_tokens <= 0 || num_tokens > 256)
-    return set_error(KRT_ERR_UNSUPPORTED, "%s: num_tokens must be in 1..256", name);
+  if (num_tokens <= 0 || num_tokens > max_tokens)
+    return set_error(KRT_ERR_UNSUPPORTED, "%s: num_tokens must be in 1..%d", name, max_tokens);
   if (d_model <= 0 || d_model % kBK != 0)
     return set_error(KRT_ERR_UNSUPPORTED, "%s: d_model must be a positive multiple of 64", name);
   if (x_stride < d_model || x_stride % 8 != 0)
@@ -575,7 +587,7 @@ int projection_params(PagedParams& p, const char* name, const void* x, const voi
 }  // namespace
 
 extern "C" size_t krt_projection_workspace_size(int32_t num_tokens, int32_t d_model) {
-  if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0) return 0;
+  if (num_tokens <= 0 || num_tokens > kMaxPromptTokens || d_model <= 0) return 0;
   return proj_ws_layout(num_tokens, d_model).total;
 }
 
@@ -584,7 +596,7 @@ extern "C" int krt_gate_up_swiglu(const krt_gate_up_args* a, void* stream) {
   if (!a) return set_error(KRT_ERR_INVALID, "%s: args is NULL", name);
   PagedParams p;
   int rc = projection_params(p, name, a->x, a->rms_weight, a->gate_up_weight, a->num_tokens, a->d_model, a->x_stride,
-                             a->eps, a->workspace, a->workspace_bytes);
+                             a->eps, a->workspace, a->workspace_bytes, kMaxPromptTokens);
   if (rc) return rc;
   if (!a->act) return set_error(KRT_ERR_INVALID, "%s: act is NULL", name);
   if (a->inter_local <= 0 || a->inter_local % 64 != 0)

@@ -112,6 +112,8 @@ inline WsLayout ws_layout(int T, int D) {
 // partials of the persistent projection kernel (at most kSkMaxCtas CTAs,
 // one 128-row partial of n_pad tokens each).
 constexpr int kSkMaxCtas = 160;
+// Tokens per gate/up call (a prompt runs in 256-token blocks).
+constexpr int kMaxPromptTokens = 1 << 20;
 struct ProjWsLayout {
   WsLayout base;
   size_t flags_off, part_off, total;
@@ -120,7 +122,8 @@ inline ProjWsLayout proj_ws_layout(int T, int D) {
   auto up = [](size_t v) { return (v + 1023) & ~size_t(1023); };
   ProjWsLayout l;
   l.base = ws_layout(T, D);
-  const size_t n_pad = ((size_t)T + 15) / 16 * 16;
+  // partials cover at most one 256-token block (stream-K runs at decode sizes only)
+  const size_t n_pad = ((size_t)(T < 256 ? T : 256) + 15) / 16 * 16;
   l.flags_off = l.base.total;
   l.part_off = up(l.flags_off + 4 * (size_t)kSkMaxCtas);
   l.total = up(l.part_off + (size_t)kSkMaxCtas * n_pad * 128 * 4);

@@ -76,6 +76,18 @@ class PagedAttentionArgs(ctypes.Structure):
     ]
 
 
+class PagedPrefillAttentionArgs(ctypes.Structure):
+    """krt_paged_prefill_attention_args"""
+    _fields_ = [
+        ("q", _vp), ("out", _vp), ("kv_pool", _vp), ("block_table", _vp), ("q_start", _vp), ("q_pos0", _vp),
+        ("num_seqs", _i32), ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32),
+        ("q_stride", _i32), ("out_stride", _i32),
+        ("block_table_stride", _i32), ("num_blocks", _i32), ("tokens_per_block", _i32),
+        ("max_q_len", _i32), ("scale", ctypes.c_float),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 class GateUpArgs(ctypes.Structure):
     """krt_gate_up_args"""
     _fields_ = [
@@ -130,6 +142,8 @@ SIGNATURES = {
     "krt_rowparallel_gemm_ar": (ctypes.c_int, [_vp, ctypes.POINTER(GemmArArgs), _vp]),
     "krt_paged_attention_workspace_size": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "krt_paged_attention_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttentionArgs), _vp]),
+    "krt_paged_attention_prefill_workspace_size": (ctypes.c_size_t, []),
+    "krt_paged_attention_prefill": (ctypes.c_int, [ctypes.POINTER(PagedPrefillAttentionArgs), _vp]),
     "krt_projection_workspace_size": (ctypes.c_size_t, [_i32, _i32]),
     "krt_gate_up_swiglu": (ctypes.c_int, [ctypes.POINTER(GateUpArgs), _vp]),
     "krt_lm_head_argmax": (ctypes.c_int, [ctypes.POINTER(LmHeadArgs), _vp]),
@@ -347,6 +361,31 @@ def attention_args(q, kv_pool, block_table, seq_lens, out, n_heads, n_kv_heads, 
 
 def paged_attention_decode(args, stream=None):
     check(lib().krt_paged_attention_decode(ctypes.byref(args), _stream(stream)))
+
+
+def prefill_attention_workspace_bytes():
+    return int(lib().krt_paged_attention_prefill_workspace_size())
+
+
+def prefill_attention_args(q, kv_pool, block_table, q_start, q_pos0, out, n_heads, n_kv_heads, num_blocks,
+                           tokens_per_block, max_q_len, workspace, scale=0.0, head_dim=128):
+    """q / out: bf16 [T, >= n_heads * 128] (sequence s's query rows q_start[s] ..
+    q_start[s + 1] - 1); q_start int32 [num_seqs + 1]; q_pos0 int32 [num_seqs]."""
+    a = PagedPrefillAttentionArgs()
+    a.q, a.out, a.kv_pool, a.block_table = _ptr(q), _ptr(out), _ptr(kv_pool), _ptr(block_table)
+    a.q_start, a.q_pos0 = _ptr(q_start), _ptr(q_pos0)
+    a.num_seqs, a.n_heads, a.n_kv_heads, a.head_dim = int(q_pos0.shape[0]), int(n_heads), int(n_kv_heads), int(head_dim)
+    a.q_stride, a.out_stride = int(q.stride(0)), int(out.stride(0))
+    a.block_table_stride, a.num_blocks = int(block_table.stride(0)), int(num_blocks)
+    a.tokens_per_block, a.max_q_len, a.scale = int(tokens_per_block), int(max_q_len), float(scale)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel() * workspace.element_size()
+    a._refs = (q, kv_pool, block_table, q_start, q_pos0, out, workspace)
+    return a
+
+
+def paged_attention_prefill(args, stream=None):
+    check(lib().krt_paged_attention_prefill(ctypes.byref(args), _stream(stream)))
 
 
 # ------------------------------------------------- rest of the decode step

@@ -286,6 +286,76 @@ class PagedDecoder:
             self.step()
         return g
 
+    # ------------------------------------------------------------ prefill
+    def prefill(self, prompts, group=8):
+        """Process the prompts of all `batch` sequences (prompts[b]: token ids
+        of sequence b, positions 0 .. len - 1), `group` sequences at a time.
+        Per layer: the prefill QKV kernel (K/V of every prompt token into the
+        pool), causal prefill attention over the pool, o_proj + allreduce +
+        residual, gate/up + SwiGLU over the whole group's tokens, down_proj +
+        allreduce + residual.  Then the lm_head on each prompt's last token
+        and the greedy step: afterwards the next step() processes the chosen
+        token at position len(prompts[b]).  The reference's generation loop
+        instead re-runs the model over the whole token list for every new
+        token (python/kinetic_rt/orchestrator.py:419-448).  Returns the chosen
+        tokens (device int32 [batch])."""
+        torch, s, w = self.torch, self.shape, self.w
+        if len(prompts) != self.B:
+            raise ValueError(f"prefill needs one prompt per sequence ({self.B}), got {len(prompts)}")
+        dev = self.h.device
+        lens = [len(p) for p in prompts]
+        if min(lens) < 1 or max(lens) >= self.max_seq_len:
+            raise ValueError("prompt lengths must be in 1 .. max_seq_len - 1")
+        D, hd, tpb = s.d_model, s.head_dim, s.tokens_per_block
+        c = self.comm_handle
+        last_h = torch.empty(self.B, D, dtype=torch.bfloat16, device=dev)
+        for g0 in range(0, self.B, group):
+            seqs = list(range(g0, min(self.B, g0 + group)))
+            glens = [lens[b] for b in seqs]
+            T = sum(glens)
+            ids = torch.cat([torch.as_tensor(prompts[b], dtype=torch.int64).reshape(-1) for b in seqs]).to(dev)
+            token_seq = torch.cat([torch.full((n,), b, dtype=torch.int32) for b, n in zip(seqs, glens)]).to(dev)
+            positions = torch.cat([torch.arange(n, dtype=torch.int32) for n in glens]).to(dev)
+            starts = [0]
+            for n in glens:
+                starts.append(starts[-1] + n)
+            q_start = torch.tensor(starts, dtype=torch.int32, device=dev)
+            q_pos0 = torch.zeros(len(seqs), dtype=torch.int32, device=dev)
+            table = self.block_table[seqs[0]:seqs[-1] + 1].contiguous()
+            hp = w.embed.index_select(0, ids).contiguous()
+            qp = torch.empty(T, self.hq * hd, dtype=torch.bfloat16, device=dev)
+            attnp = torch.empty_like(qp)
+            actp = torch.empty(T, self.ir, dtype=torch.bfloat16, device=dev)
+            z = lambda n: torch.zeros(n, dtype=torch.uint8, device=dev)
+            ws_q = z(_lib.prefill_workspace_bytes(T, D, self.hq, self.hkv))
+            ws_a = z(_lib.prefill_attention_workspace_bytes())
+            ws_p = z(_lib.projection_workspace_bytes(T, D))
+            ws_g = z(_lib.gemm_ar_workspace_bytes())
+            for li in range(s.n_layers):
+                _lib.qkv_rope_prefill(_lib.paged_args(hp, w.qkv[li], None, w.g_attn[li], self.cos, self.sin, positions,
+                                                      token_seq, self.block_table, self.pools[li], qp, self.hq,
+                                                      self.hkv, self.num_blocks, tpb, ws_q, eps=s.eps))
+                _lib.paged_attention_prefill(_lib.prefill_attention_args(qp, self.pools[li], table, q_start, q_pos0,
+                                                                         attnp, self.hq, self.hkv, self.num_blocks,
+                                                                         tpb, max(glens), ws_a))
+                _lib.rowparallel_gemm_ar(c, _lib.gemm_ar_args(attnp, w.o[li], hp, ws_g, residual=hp))
+                _lib.gate_up_swiglu(_lib.gate_up_args(hp, w.g_mlp[li], w.gate_up[li], actp, ws_p, eps=s.eps))
+                _lib.rowparallel_gemm_ar(c, _lib.gemm_ar_args(actp, w.down[li], hp, ws_g, residual=hp))
+            last_h[seqs[0]:seqs[-1] + 1] = hp.index_select(0, (q_start[1:] - 1).long())
+            for ws in (ws_q, ws_a, ws_p, ws_g):
+                rc, bits = _lib.read_status(ws)
+                if rc != 0:
+                    raise RuntimeError(f"prefill kernel status {bits:#x}")
+            del hp, qp, attnp, actp
+        # the last prompt token's state, then lm_head + greedy step as in a decode step
+        L = torch.tensor(lens, dtype=torch.int32, device=dev)
+        self.h.copy_(last_h)
+        self.positions.copy_(L - 1)
+        self.seq_lens.copy_(L)
+        self.next_input.fill_(-1)
+        self.tail()
+        return self.tokens
+
     # ------------------------------------------------------------ state
     def start(self, start_tokens, positions):
         """Next step processes token start_tokens[b] at position positions[b]."""

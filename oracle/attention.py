@@ -42,3 +42,22 @@ def paged_decode_attention(q, pool, block_table, seq_lens, n_heads, n_kv_heads, 
             w /= w.sum()
             out[s, h] = w @ v[:, kv].astype(np.float64)
     return out
+
+
+def paged_prefill_attention(q, pool, block_table, q_start, q_pos0, n_heads, n_kv_heads, tokens_per_block,
+                            scale=None):
+    """Causal attention of prompt tokens over the pool: sequence s's query rows
+    q_start[s] .. q_start[s + 1] - 1 sit at positions q_pos0[s] + i and attend
+    to the sequence's pool tokens 0 .. q_pos0[s] + i.  q [T, n_heads, 128];
+    returns [T, n_heads, 128] float64.  Each query row is the decode case with
+    seq_len = its position + 1 (paged_decode_attention)."""
+    q = np.asarray(q, dtype=np.float64)
+    out = np.zeros(q.shape, dtype=np.float64)
+    for s in range(len(q_pos0)):
+        rows = list(range(int(q_start[s]), int(q_start[s + 1])))
+        if not rows:
+            continue
+        lens = [int(q_pos0[s]) + i + 1 for i in range(len(rows))]
+        tables = np.repeat(np.asarray(block_table)[s:s + 1], len(rows), axis=0)
+        out[rows] = paged_decode_attention(q[rows], pool, tables, lens, n_heads, n_kv_heads, tokens_per_block, scale)
+    return out

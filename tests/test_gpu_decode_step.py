@@ -46,13 +46,13 @@ def _projection_kernel(monkeypatch, mode):
 
 @pytest.mark.parametrize("mode,T,I", [("splitk", 37, 320), ("tiles", 37, 320), ("streamk", 37, 320),
                                       ("auto", 128, 9600), ("tiles", 200, 704), ("streamk", 200, 704),
-                                      ("streamk", 64, 9600)])
+                                      ("streamk", 64, 9600), ("auto", 700, 704), ("auto", 300, 9600)])
 def test_gate_up_swiglu(torch_cuda, monkeypatch, mode, T, I):
     """Split-K kernel (few tiles) and the persistent kernel: whole tiles (150
     tiles on 148 SMs gives two tiles to some CTAs, through both TMEM buffers)
     and stream-K (5 tiles of 4 k-boxes on 20 CTAs: every tile is one head
     and three partials; 150 tiles on 148 CTAs: runs of 4-5 boxes crossing
-    tile boundaries)."""
+    tile boundaries); prompts of 300 and 700 tokens run in 256-token blocks."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
     _projection_kernel(monkeypatch, mode)
@@ -262,6 +262,66 @@ def test_decode_steps_seventy_b_rank_shapes(torch_cuda):
     10 QKV tiles over 128 k-blocks, a single KV head per pool, 8192-wide
     GEMM outputs; two graph-replayed steps against the oracle."""
     run_decoder_against_oracle(torch_cuda, steps=2, model=dict(L=1, D=8192, H=8, KV=1, I=3584))
+
+
+@pytest.mark.parametrize("lens", [(37, 37, 37), (5, 300, 64)])
+def test_prefill_then_decode_matches_oracle(torch_cuda, lens):
+    """PagedDecoder.prefill of a tiny two-layer model (prompt K/V into the
+    pools through the prefill QKV and causal prefill attention kernels, the
+    MLP over whole prompts) against the oracle fed the prompts token by token:
+    the K/V at every prompt position, the first chosen token (near-ties
+    excepted), then two graph-replayed decode steps.  A group holding the
+    300-token prompt runs gate/up in 256-token blocks and the row-parallel
+    GEMMs in 256-token launches."""
+    torch = torch_cuda
+    from python.kinetic_rt.decoder import PagedDecoder, RankWeights
+    rng = np.random.Generator(np.random.PCG64(21))
+    shape, full = tiny_model(rng)
+    B, max_len = len(lens), max(lens) + 16
+    w = RankWeights.from_full(torch, shape, full, 0, 1)
+    dec = PagedDecoder(torch, shape, w, B, max_len)
+    prompts = [rng.integers(0, shape.vocab, size=n) for n in lens]
+    got_tok = dec.prefill(prompts, group=2).cpu().numpy()
+    dec.check_status()
+    table = dec.block_table.cpu().numpy()
+    cos, sin = fused_layer.rope_tables(np.arange(max_len), 128, shape.rope_theta)
+    pools = [np.zeros((dec.num_blocks, 16, 2, shape.n_kv_heads, 128), np.float32) for _ in range(shape.n_layers)]
+    # the oracle one position at a time; a sequence whose prompt has ended
+    # keeps re-running its last token (its K/V slot is rewritten identically)
+    last_logits = [None] * B
+    for p in range(max(lens)):
+        pos = np.array([min(p, n - 1) for n in lens])
+        h = np.stack([full["embed"][prompts[b][pos[b]]] for b in range(B)])
+        logits, _, _ = odec.decode_step(full, h, pos, table, pools, cos, sin, shape.n_heads, shape.n_kv_heads, 16)
+        for b in range(B):
+            if p == lens[b] - 1:
+                last_logits[b] = logits[b]
+    for li in range(shape.n_layers):
+        got_pool = dec.pools[li].float().cpu().numpy().reshape(dec.num_blocks, 16, 2, shape.n_kv_heads, 128)
+        for b in range(B):
+            for p in range(lens[b]):
+                blk, off = table[b][p // 16], p % 16
+                np.testing.assert_allclose(got_pool[blk, off], pools[li][blk, off], atol=ATOL, rtol=RTOL)
+    want = np.array([int(np.argmax(lg)) for lg in last_logits])
+    for b in range(B):
+        top2 = np.sort(last_logits[b])[-2:]
+        assert got_tok[b] == want[b] or top2[1] - top2[0] < ATOL + RTOL * abs(top2[1]), (b, got_tok[b], want[b])
+    # continue from the oracle's tokens on both sides
+    dec.h.copy_(w.embed.index_select(0, torch.as_tensor(want, device="cuda")))
+    graph = dec.capture()
+    h, pos = full["embed"][want], np.array(lens)
+    for step in range(2):
+        logits, tok, h_next = odec.decode_step(full, h, pos, table, pools, cos, sin, shape.n_heads,
+                                               shape.n_kv_heads, 16)
+        dec.next_input.copy_(torch.from_numpy(tok.astype(np.int32)))
+        graph.replay()
+        dec.check_status()
+        gt = dec.tokens.cpu().numpy()
+        top2 = np.sort(logits, -1)[:, -2:]
+        near_tie = top2[:, 1] - top2[:, 0] < ATOL + RTOL * np.abs(top2[:, 1])
+        assert np.all((gt == tok) | near_tie), (step, gt, tok)
+        h, pos = h_next, pos + 1
+    del graph
 
 
 def test_runtime_generate_matches_oracle(torch_cuda):
