@@ -9,8 +9,10 @@
 // Additions: BlockManager, descriptor fields of the paged path, and the
 // peer-buffer and fused GEMM + allreduce methods of Communicator.
 #include <pybind11/pybind11.h>
+#include <pybind11/functional.h>
 #include <pybind11/stl.h>
 
+#include <chrono>
 #include <cstdint>
 #include <cstdio>
 #include <stdexcept>
@@ -22,6 +24,7 @@
 #include "BlockManager.h"
 #include "Communicator.h"
 #include "GraphWrapper.h"
+#include "RequestContext.h"
 #include "Router.h"
 
 namespace py = pybind11;
@@ -382,4 +385,79 @@ PYBIND11_MODULE(KRT_MODULE_NAME, m) {
   py::class_<InferenceWorker>(m, "InferenceWorker", py::module_local())
       .def(py::init<InferenceQueue&, HardwareRouter&>(), py::arg("queue"), py::arg("router"), py::keep_alive<1, 2>(),
            py::keep_alive<1, 3>());
+
+  // ---- per-request lifecycle (RequestContext.h)
+  py::enum_<RequestState>(m, "RequestState", py::module_local())
+      .value("RECEIVED", RequestState::RECEIVED).value("VALIDATED", RequestState::VALIDATED)
+      .value("TOKENIZED", RequestState::TOKENIZED).value("ENQUEUED", RequestState::ENQUEUED)
+      .value("PREFILL", RequestState::PREFILL).value("DECODE", RequestState::DECODE)
+      .value("STREAMING", RequestState::STREAMING).value("COMPLETE", RequestState::COMPLETE)
+      .value("CANCELLED", RequestState::CANCELLED).value("TIMED_OUT", RequestState::TIMED_OUT)
+      .value("FAILED", RequestState::FAILED);
+  py::enum_<CompletionReason>(m, "CompletionReason", py::module_local())
+      .value("STREAMING", CompletionReason::STREAMING).value("EOS", CompletionReason::EOS)
+      .value("STOP_TOKEN", CompletionReason::STOP_TOKEN).value("LENGTH", CompletionReason::LENGTH)
+      .value("CANCELLED", CompletionReason::CANCELLED).value("TIMEOUT", CompletionReason::TIMEOUT)
+      .value("ERROR", CompletionReason::ERROR);
+  py::enum_<Owner>(m, "Owner", py::module_local())
+      .value("Ingress", Owner::Ingress).value("Scheduler", Owner::Scheduler)
+      .value("Executor", Owner::Executor).value("Backend", Owner::Backend);
+  auto rc_error = py::register_local_exception<RequestContextError>(m, "RequestContextError", PyExc_RuntimeError);
+  py::register_local_exception<InvalidStateTransitionError>(m, "InvalidStateTransitionError", rc_error);
+  py::register_local_exception<RequestOwnershipError>(m, "RequestOwnershipError", rc_error);
+  py::class_<RequestContext>(m, "RequestContext", py::module_local())
+      .def(py::init([](std::string request_id, std::string prompt_text, std::vector<int32_t> prompt_tokens,
+                       int max_new_tokens, float temperature, float top_p, int top_k,
+                       std::vector<int32_t> stop_token_ids, std::string backend_hint, double timeout_s,
+                       Owner initial_owner) {
+             RequestContext::Config c;
+             c.request_id = std::move(request_id);
+             c.prompt_text = std::move(prompt_text);
+             c.prompt_tokens = std::move(prompt_tokens);
+             c.max_new_tokens = max_new_tokens;
+             c.temperature = temperature;
+             c.top_p = top_p;
+             c.top_k = top_k;
+             c.stop_token_ids = std::move(stop_token_ids);
+             c.backend_hint = std::move(backend_hint);
+             c.timeout = std::chrono::duration_cast<RequestContext::Clock::duration>(
+                 std::chrono::duration<double>(timeout_s));
+             c.initial_owner = initial_owner;
+             return new RequestContext(std::move(c));
+           }),
+           py::arg("request_id"), py::arg("prompt_text") = "", py::arg("prompt_tokens") = std::vector<int32_t>{},
+           py::arg("max_new_tokens") = 0, py::arg("temperature") = 1.0f, py::arg("top_p") = 1.0f,
+           py::arg("top_k") = 0, py::arg("stop_token_ids") = std::vector<int32_t>{}, py::arg("backend_hint") = "",
+           py::arg("timeout_s") = 0.0, py::arg("initial_owner") = Owner::Ingress)
+      .def_property_readonly("request_id", &RequestContext::request_id)
+      .def_property_readonly("prompt_text", &RequestContext::prompt_text)
+      .def_property_readonly("prompt_tokens", &RequestContext::prompt_tokens)
+      .def_property_readonly("max_new_tokens", &RequestContext::max_new_tokens)
+      .def_property_readonly("stop_token_ids", &RequestContext::stop_token_ids)
+      .def("is_valid", &RequestContext::is_valid)
+      .def("ensure_executable", &RequestContext::ensure_executable)
+      .def("state", &RequestContext::state)
+      .def("can_transition_to", &RequestContext::can_transition_to)
+      .def("transition_to", &RequestContext::transition_to)
+      .def("is_terminal", py::overload_cast<>(&RequestContext::is_terminal, py::const_))
+      .def("request_cancellation", &RequestContext::request_cancellation)
+      .def("is_cancellation_requested", &RequestContext::is_cancellation_requested)
+      .def("acknowledge_cancellation", &RequestContext::acknowledge_cancellation)
+      .def("has_deadline", &RequestContext::has_deadline)
+      .def("is_expired", [](const RequestContext& r) { return r.is_expired(); })
+      .def("acknowledge_timeout", [](RequestContext& r) { r.acknowledge_timeout(); })
+      .def("current_owner", &RequestContext::current_owner)
+      .def("transfer_ownership", &RequestContext::transfer_ownership, py::arg("new_owner"),
+           py::arg("expected_current_owner"))
+      .def("append_generated_token", &RequestContext::append_generated_token)
+      .def("generated_tokens", &RequestContext::generated_tokens)
+      .def("set_kv_block_ids", &RequestContext::set_kv_block_ids)
+      .def("kv_block_ids", &RequestContext::kv_block_ids)
+      .def("set_finish_reason", &RequestContext::set_finish_reason)
+      .def("finish_reason", &RequestContext::finish_reason)
+      .def("set_error_code", &RequestContext::set_error_code)
+      .def("error_code", &RequestContext::error_code)
+      .def("register_cleanup_callback", &RequestContext::register_cleanup_callback)
+      .def("is_cleaned_up", &RequestContext::is_cleaned_up)
+      .def("cleanup", &RequestContext::cleanup);
 }

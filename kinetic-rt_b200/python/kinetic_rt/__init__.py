@@ -29,6 +29,13 @@ TensorDescriptor = _native.TensorDescriptor
 DataType = _native.DataType
 KernelLaunchDescriptor = _native.KernelLaunchDescriptor
 BlockManager = _native.BlockManager
+RequestContext = _native.RequestContext
+RequestState = _native.RequestState
+CompletionReason = _native.CompletionReason
+Owner = _native.Owner
+RequestContextError = _native.RequestContextError
+InvalidStateTransitionError = _native.InvalidStateTransitionError
+RequestOwnershipError = _native.RequestOwnershipError
 MOCK_CUDA = _native.MOCK_CUDA
 
 

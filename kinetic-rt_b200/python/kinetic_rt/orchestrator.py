@@ -134,18 +134,52 @@ class KineticRuntime:
         ids = self.tokenizer.encode(prompt) if getattr(self, "tokenizer", None) else list(prompt.encode("utf-8"))
         return [int(t) for t in ids]
 
-    def generate_ids(self, prompt_ids, max_new_tokens=10):
+    def generate_ids(self, prompt_ids, max_new_tokens=10, request=None):
         """Greedy continuation of `prompt_ids` (a list of ints): the prompt is
         fed one token per decode step (its K/V cached as it goes), then each
         step's argmax (orchestrator.py:442-444) becomes the next input.
-        Returns the new token ids."""
+        Returns the new token ids.
+
+        With `request` (a RequestContext of the runtime module) the call drives
+        its lifecycle: RECEIVED -> VALIDATED -> TOKENIZED -> ENQUEUED (ownership
+        to the executor) -> PREFILL while the prompt is fed -> DECODE <->
+        STREAMING per generated token (each appended to the context) ->
+        COMPLETE with reason LENGTH (the context's max_new_tokens, when set,
+        replaces the argument) or STOP_TOKEN (a token in its stop_token_ids).
+        Between steps it honours a cancellation request (acknowledged ->
+        CANCELLED) and the deadline (-> TIMED_OUT), returning the tokens made
+        so far; an exception moves the context to FAILED.  The context records
+        the sequence's KV block ids and is cleaned up when it ends."""
         dec = getattr(self, "decoder", None)
         if dec is None:
             raise RuntimeConfigurationError("no decoder attached (KineticRuntime.attach_decoder)")
+        if request is not None and request.max_new_tokens > 0:
+            max_new_tokens = request.max_new_tokens
         if not prompt_ids:
             raise RuntimeConfigurationError("empty prompt")
         if len(prompt_ids) + max_new_tokens > dec.max_seq_len:
             raise ContextWindowExceededError("prompt and new tokens exceed the decoder's max_seq_len")
+        if request is None:
+            return self._generate(dec, prompt_ids, max_new_tokens, None)
+        from . import RequestState as S, Owner, CompletionReason
+        try:
+            for st in (S.VALIDATED, S.TOKENIZED, S.ENQUEUED):
+                request.transition_to(st)
+            request.transfer_ownership(Owner.Executor, request.current_owner())
+            request.set_kv_block_ids([int(b) for b in dec.block_table[0].tolist()])
+            request.transition_to(S.PREFILL)
+            out = self._generate(dec, prompt_ids, max_new_tokens, request)
+        except Exception:
+            if not request.is_terminal():
+                request.set_error_code(1)
+                request.set_finish_reason(CompletionReason.ERROR)
+                request.transition_to(S.FAILED)
+            request.cleanup()
+            raise
+        request.cleanup()
+        return out
+
+    def _generate(self, dec, prompt_ids, max_new_tokens, request):
         torch = dec.torch
         dec.start([prompt_ids[0]], [0])
         if self._graph is None:
@@ -153,15 +187,44 @@ class KineticRuntime:
         steps = len(prompt_ids) - 1 + max_new_tokens
         # one pinned slot per step: a slot is not rewritten while its copy may still be queued
         feed = torch.tensor([prompt_ids[i + 1] if i + 1 < len(prompt_ids) else -1 for i in range(steps)],
-                            dtype=torch.int32).pin_memory()
+                            dtype=torch.int32)
+        if torch.cuda.is_available():
+            feed = feed.pin_memory()
+        stop = set(request.stop_token_ids) if request is not None else set()
         out = []
         for i in range(steps):
+            if request is not None and self._request_over(request):
+                break
             dec.next_input.copy_(feed[i:i + 1], non_blocking=True)
             self._graph.replay()
             if i + 1 >= len(prompt_ids):
-                out.append(int(dec.tokens[0].item()))
+                tok = int(dec.tokens[0].item())
+                out.append(tok)
+                if request is not None:
+                    from . import RequestState as S, CompletionReason
+                    if request.state() == S.PREFILL:
+                        request.transition_to(S.DECODE)
+                    request.append_generated_token(tok)
+                    request.transition_to(S.STREAMING)
+                    if tok in stop or len(out) == max_new_tokens:
+                        request.set_finish_reason(CompletionReason.STOP_TOKEN if tok in stop
+                                                  else CompletionReason.LENGTH)
+                        request.transition_to(S.COMPLETE)
+                        break
+                    request.transition_to(S.DECODE)
         dec.check_status()
         return out
+
+    @staticmethod
+    def _request_over(request):
+        """Cancellation and deadline checks between decode steps."""
+        if request.is_cancellation_requested():
+            request.acknowledge_cancellation()
+            return True
+        if request.is_expired():
+            request.acknowledge_timeout()
+            return True
+        return False
 
     def generate(self, prompt, max_new_tokens=10):
         """Text in, text out (the reference's generate, orchestrator.py:419-448)."""

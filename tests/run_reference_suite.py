@@ -12,6 +12,10 @@ edited; the path comes only from KINETIC_REFERENCE.
 --gpu   tests/test_fusion.py against the CUDA runtime (python.kinetic_rt._core):
         the .kin bridge and the known-answer math through the
         fused_rmsnorm_qkv_rope[grid](...) call with CPU tensors (needs a B200).
+--cpp   tests/test_request_context.cpp, the reference's C++ test of its
+        RequestContext, compiled with g++ against this build's
+        kinetic-rt_b200/csrc/runtime/RequestContext.cpp (its header found first on
+        the include path) and run.
 --host  the tests that drive the runtime with fake stream pointers and host
         buffers (test_graph, test_aot, test_validation, test_distributed,
         test_hardware_probe) against the host-only build
@@ -33,10 +37,32 @@ GPU_TESTS = ["test_fusion.py"]
 HOST_TESTS = ["test_graph.py", "test_aot.py", "test_validation.py", "test_distributed.py", "test_hardware_probe.py"]
 
 
+CPP_TESTS = ["test_request_context.cpp"]
+
+
+def run_cpp(tests_dir):
+    """Compile and run the reference's C++ RequestContext test against this
+    build's implementation; returns the test binary's exit status."""
+    runtime = os.path.join(PKG_ROOT, "csrc", "runtime")
+    src = os.path.join(tests_dir, CPP_TESTS[0])
+    if not os.path.exists(src):
+        print(f"no {CPP_TESTS[0]} under {tests_dir}", file=sys.stderr)
+        return 4
+    with tempfile.TemporaryDirectory() as scratch:
+        exe = os.path.join(scratch, "test_request_context")
+        rc = subprocess.call(["g++", "-O1", "-std=c++17", "-I", runtime, src,
+                              os.path.join(runtime, "RequestContext.cpp"), "-o", exe, "-lpthread"])
+        if rc != 0:
+            return rc
+        return subprocess.call([exe], cwd=scratch)
+
+
 def run(tests_dir, which, extra=()):
     tests_dir = os.path.abspath(tests_dir)  # pytest runs from a scratch directory
     if os.path.isdir(os.path.join(tests_dir, "tests")):
         tests_dir = os.path.join(tests_dir, "tests")
+    if which == "cpp":
+        return run_cpp(tests_dir)
     files = [os.path.join(tests_dir, f) for f in (GPU_TESTS if which == "gpu" else HOST_TESTS)]
     files = [f for f in files if os.path.exists(f)]
     if not files:
@@ -62,8 +88,8 @@ def main():
     if not tests_dir:
         print("set KINETIC_REFERENCE to the reference's tests directory", file=sys.stderr)
         return 2
-    which = "gpu" if "--gpu" in sys.argv else "host"
-    return run(tests_dir, which, [a for a in sys.argv[1:] if a not in ("--gpu", "--host")])
+    which = "gpu" if "--gpu" in sys.argv else "cpp" if "--cpp" in sys.argv else "host"
+    return run(tests_dir, which, [a for a in sys.argv[1:] if a not in ("--gpu", "--host", "--cpp")])
 
 
 if __name__ == "__main__":

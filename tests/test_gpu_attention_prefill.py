@@ -106,5 +106,5 @@ def test_prefill_attention_bad_block_sets_status(torch_cuda):
                                     20, ws)
     _lib.paged_attention_prefill(a)
     rc, bits = _lib.read_status(ws)
-    assert rc == 0 and bits & 8
+    assert bits == 8  # the bad-block bit alone (krt_read_status also returns an error code for it)
     assert torch.isfinite(out.float()).all()

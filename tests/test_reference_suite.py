@@ -23,6 +23,12 @@ def test_reference_host_tests_pass_unmodified():
     assert _run("host") == 0
 
 
+def test_reference_request_context_cpp_test_passes_unmodified():
+    """The reference's tests/test_request_context.cpp against this build's
+    RequestContext (g++, no GPU)."""
+    assert _run("cpp") == 0
+
+
 @pytest.mark.gpu
 def test_reference_fusion_test_passes_unmodified():
     pytest.importorskip("torch")
