@@ -159,3 +159,32 @@ def test_read_status_rejects_null():
     bits = ctypes.c_int32(0)
     rc, msg = _call("krt_read_status", None, None, ctypes.byref(bits))
     assert rc == _lib.KRT_ERR_INVALID and "NULL" in msg
+
+
+def _prefill_attn(**over):
+    a = _lib.PagedPrefillAttentionArgs()
+    for name in ("q", "out", "kv_pool", "block_table", "q_start", "q_pos0", "workspace"):
+        setattr(a, name, FAKE)
+    a.num_seqs, a.n_heads, a.n_kv_heads, a.head_dim = 8, 32, 8, 128
+    a.q_stride, a.out_stride = 4096, 4096
+    a.block_table_stride, a.num_blocks, a.tokens_per_block = 128, 1024, 16
+    a.max_q_len, a.workspace_bytes = 2048, 1 << 20
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("over,code,text", [
+    (dict(q=0), _lib.KRT_ERR_INVALID, "NULL"),
+    (dict(head_dim=64), _lib.KRT_ERR_UNSUPPORTED, "head_dim"),
+    (dict(n_heads=24, n_kv_heads=8), _lib.KRT_ERR_UNSUPPORTED, "1, 2, 4, 8 or 16"),
+    (dict(n_heads=30, n_kv_heads=8), _lib.KRT_ERR_INVALID, "n_kv_heads"),
+    (dict(tokens_per_block=8), _lib.KRT_ERR_UNSUPPORTED, "multiple of 16"),
+    (dict(q_stride=1000), _lib.KRT_ERR_INVALID, "strides"),
+    (dict(max_q_len=0), _lib.KRT_ERR_INVALID, "positive"),
+    (dict(workspace_bytes=16), _lib.KRT_ERR_WORKSPACE, "workspace"),
+])
+def test_prefill_attention_rejects_bad_arguments(over, code, text):
+    a = _prefill_attn(**over)
+    rc, msg = _call("krt_paged_attention_prefill", ctypes.byref(a), None)
+    assert rc == code and text in msg and "krt_paged_attention_prefill" in msg, (rc, msg)
