@@ -17,13 +17,15 @@
 //     range first; a tile is 128 rows = (128 / G) consecutive query tokens x
 //     the G query heads of one KV head;
 //   * a producer warp streams the tile's causal range of K/V in 16-token
-//     chunks through a 4-stage ring (one 5-D TMA box = K and V of one KV head
+//     chunks through an 8-stage ring (one 5-D TMA box = K and V of one KV head
 //     for 16 tokens, 8 KB, the decode kernel's tensor map);
 //   * eight compute warps hold 16 rows each (16 / G tokens x G heads) and run
-//     Q K^T and P V with mma.sync m16n8k16 and an online softmax in base 2;
-//     keys past a row's position are masked, and a warp skips the math of
-//     chunks that lie wholly past its last token (it still waits for and
-//     releases every stage, so releases stay in step with the fills);
+//     Q K^T and P V with mma.sync m16n8k16 over blocks of four chunks (64
+//     keys) with one online-softmax update (base 2) per block, so the output
+//     rescale and the row reductions are paid once per 64 keys; keys past a
+//     row's position are masked, and a warp skips the math of blocks that lie
+//     wholly past its last token (it still waits for and releases every
+//     stage, so releases stay in step with the fills);
 //   * every wait is bounded; a block-table entry out of range reads token 0,
 //     masks the chunk and sets status bit 8, as does a sequence with more
 //     query tokens than max_q_len (the rows past it are left unwritten).
@@ -42,7 +44,8 @@ namespace krt {
 constexpr int kPfaWarps = 8;                      // compute warps
 constexpr int kPfaThreads = 32 * (kPfaWarps + 1);  // + the producer warp
 constexpr int kPfaRows = 16 * kPfaWarps;           // query rows per CTA
-constexpr int kPfaStages = 4;
+constexpr int kPfaStages = 8;                     // two softmax blocks in flight
+constexpr int kPfaBlk = 4;                         // 16-token chunks per softmax update (64 keys)
 constexpr int kPfaChunk = 16;                      // tokens per TMA box
 constexpr uint32_t kPfaStageBytes = 8192;          // K and V of 16 tokens, one KV head
 
@@ -193,49 +196,61 @@ __global__ void __launch_bounds__(kPfaThreads, 1)
   float m_r[2] = {-INFINITY, -INFINITY};
   float l_r[2] = {0.f, 0.f};
   const uint32_t stages = smem_u32(smem);
-  int s = 0;
-  uint32_t ph = 0;
+  const int n_blocks = (n_chunks + kPfaBlk - 1) / kPfaBlk;
   bool ok = true;
-  for (int k = 0; k < n_chunks; ++k) {
-    // Every warp waits for every chunk, also one it has no keys for: its
-    // release of the stage must not count toward a later fill of the same
-    // stage (the producer refills a stage once all eight warps released it).
-    if (!mbar_wait_warp(&tl->full[s], ph, nullptr)) {
-      if (lane == 0) atomicOr(p.status, kStatusTimeoutFull);
-      ok = false;
-      break;
+  for (int kb = 0; kb < n_blocks; ++kb) {
+    const int k0 = kb * kPfaBlk;
+    const int nc = min(kPfaBlk, n_chunks - k0);  // chunks in this block (the last one may be short)
+    // Every warp waits for every chunk, also those it has no keys for: its
+    // release of a stage must not count toward a later fill of the same stage
+    // (the producer refills a stage once all eight warps released it).
+    for (int c = 0; c < nc && ok; ++c) {
+      const int k = k0 + c;
+      if (!mbar_wait_warp(&tl->full[k % kPfaStages], (uint32_t)(k / kPfaStages) & 1u, nullptr)) {
+        if (lane == 0) atomicOr(p.status, kStatusTimeoutFull);
+        ok = false;
+      }
     }
-    if (k < w_chunks) {
-      const uint32_t st = stages + (uint32_t)s * kPfaStageBytes;
-      const bool chunk_bad = tl->ctok[s] < 0;
-      // ---- S = Q K^T for the chunk's 16 keys
-      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (!ok) break;
+    if (k0 < w_chunks) {
+      // ---- S = Q K^T for the block's (up to) 64 keys: n-tile 2c + j holds keys 16c + 8j ..
+      float sc[2 * kPfaBlk][4];
+#pragma unroll
+      for (int jj = 0; jj < 2 * kPfaBlk; ++jj) sc[jj][0] = sc[jj][1] = sc[jj][2] = sc[jj][3] = 0.f;
       {
         const int mat = lane >> 3, r = lane & 7;
         const int tok = r + 8 * (mat >> 1);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const int half = ks >> 2, ch = 2 * (ks & 3) + (mat & 1);
-          uint32_t bf[4];
-          pfa_ldsm_x4(pfa_sw128(st + (uint32_t)half * 2048u, tok, ch), bf);
-          pfa_mma(sc[0], qa[ks], bf[0], bf[1]);
-          pfa_mma(sc[1], qa[ks], bf[2], bf[3]);
+        for (int c = 0; c < kPfaBlk; ++c) {
+          if (c >= nc) break;
+          const uint32_t st = stages + (uint32_t)((k0 + c) % kPfaStages) * kPfaStageBytes;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const int half = ks >> 2, ch = 2 * (ks & 3) + (mat & 1);
+            uint32_t bf[4];
+            pfa_ldsm_x4(pfa_sw128(st + (uint32_t)half * 2048u, tok, ch), bf);
+            pfa_mma(sc[2 * c], qa[ks], bf[0], bf[1]);
+            pfa_mma(sc[2 * c + 1], qa[ks], bf[2], bf[3]);
+          }
         }
       }
-      // ---- causal mask + online softmax (base 2)
-      const int key0 = k * kPfaChunk;
+      // ---- causal mask + one online-softmax update (base 2) for the block
       float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+      for (int c = 0; c < kPfaBlk; ++c) {
+        const bool chunk_bad = c >= nc || tl->ctok[(k0 + c) % kPfaStages] < 0;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int kp = key0 + 8 * j + 2 * t4 + (e & 1);
-          const int rr = e >> 1;
-          float v = sc[j][e] * p.scale_log2;
-          if (kp > row_pos[rr] || !row_ok[rr] || chunk_bad) v = -INFINITY;
-          sc[j][e] = v;
-          mx[rr] = fmaxf(mx[rr], v);
-        }
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kp = (k0 + c) * kPfaChunk + 8 * j + 2 * t4 + (e & 1);
+            const int rr = e >> 1;
+            float v = sc[2 * c + j][e] * p.scale_log2;
+            if (chunk_bad || kp > row_pos[rr] || !row_ok[rr]) v = -INFINITY;
+            sc[2 * c + j][e] = v;
+            mx[rr] = fmaxf(mx[rr], v);
+          }
+      }
       float corr[2];
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
@@ -245,17 +260,18 @@ __global__ void __launch_bounds__(kPfaThreads, 1)
         corr[rr] = m_new == -INFINITY ? 1.f : exp2f(m_r[rr] - m_new);
         m_r[rr] = m_new;
       }
-      float pr[2][4];
+      float lsum[2] = {0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+      for (int jj = 0; jj < 2 * kPfaBlk; ++jj)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float m = m_r[e >> 1];
-          pr[j][e] = m == -INFINITY ? 0.f : exp2f(sc[j][e] - m);
+          const float pv = m == -INFINITY ? 0.f : exp2f(sc[jj][e] - m);
+          sc[jj][e] = pv;  // probabilities in place
+          lsum[e >> 1] += pv;
         }
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr)
-        l_r[rr] = l_r[rr] * corr[rr] + pr[0][2 * rr] + pr[0][2 * rr + 1] + pr[1][2 * rr] + pr[1][2 * rr + 1];
+      for (int rr = 0; rr < 2; ++rr) l_r[rr] = l_r[rr] * corr[rr] + lsum[rr];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         o[j][0] *= corr[0];
@@ -263,33 +279,35 @@ __global__ void __launch_bounds__(kPfaThreads, 1)
         o[j][2] *= corr[1];
         o[j][3] *= corr[1];
       }
-      // ---- O += P V
-      uint32_t pa[4];
-      pa[0] = pack_bf16x2(pr[0][0], pr[0][1]);
-      pa[1] = pack_bf16x2(pr[0][2], pr[0][3]);
-      pa[2] = pack_bf16x2(pr[1][0], pr[1][1]);
-      pa[3] = pack_bf16x2(pr[1][2], pr[1][3]);
+      // ---- O += P V, one 16-key k-step per chunk
       {
         const int mat = lane >> 3, r = lane & 7;
         const int tok = r + 8 * (mat & 1);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int half = jj >> 2, ch = 2 * (jj & 3) + (mat >> 1);
-          uint32_t bf[4];
-          pfa_ldsm_x4_trans(pfa_sw128(st + 4096u + (uint32_t)half * 2048u, tok, ch), bf);
-          pfa_mma(o[2 * jj], pa, bf[0], bf[1]);
-          pfa_mma(o[2 * jj + 1], pa, bf[2], bf[3]);
+        for (int c = 0; c < kPfaBlk; ++c) {
+          if (c >= nc) break;
+          const uint32_t st = stages + (uint32_t)((k0 + c) % kPfaStages) * kPfaStageBytes;
+          uint32_t pa[4];
+          pa[0] = pack_bf16x2(sc[2 * c][0], sc[2 * c][1]);
+          pa[1] = pack_bf16x2(sc[2 * c][2], sc[2 * c][3]);
+          pa[2] = pack_bf16x2(sc[2 * c + 1][0], sc[2 * c + 1][1]);
+          pa[3] = pack_bf16x2(sc[2 * c + 1][2], sc[2 * c + 1][3]);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int half = jj >> 2, ch = 2 * (jj & 3) + (mat >> 1);
+            uint32_t bf[4];
+            pfa_ldsm_x4_trans(pfa_sw128(st + 4096u + (uint32_t)half * 2048u, tok, ch), bf);
+            pfa_mma(o[2 * jj], pa, bf[0], bf[1]);
+            pfa_mma(o[2 * jj + 1], pa, bf[2], bf[3]);
+          }
         }
       }
-      // the ldmatrix reads of the stage come before the TMA that rewrites it
+      // the ldmatrix reads of the stages come before the TMA that rewrites them
       fence_proxy_async_smem();
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&tl->empty[s]);
-    if (++s == kPfaStages) {
-      s = 0;
-      ph ^= 1u;
-    }
+    if (lane == 0)
+      for (int c = 0; c < nc; ++c) mbar_arrive(&tl->empty[(k0 + c) % kPfaStages]);
   }
   if (!ok) return;
 #pragma unroll
