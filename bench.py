@@ -1249,6 +1249,20 @@ def run_kernel(args, rank, world, local_rank):
         ws = torch.zeros(_lib.attention_workspace_bytes(B, H, KV, ctx), dtype=torch.uint8, device="cuda")
         args_list = [_lib.attention_args(q, pool, table, lens, o, H, KV, nb, BLOCK, ctx, ws)]
         call = _lib.paged_attention_decode
+    elif name == "prefill_attention":
+        # causal attention of 8 prompts x 2048 tokens (config 2's prefill) over a random pool
+        S_, L_ = 8, 2048
+        nb = S_ * L_ // BLOCK
+        pool = torch.randn(nb, BLOCK, 2 * KV * HEAD_DIM, generator=g, device="cuda").to(torch.bfloat16)
+        table = torch.randperm(nb, device="cuda").to(torch.int32).view(S_, -1)
+        q = torch.randn(S_ * L_, H * HEAD_DIM, generator=g, device="cuda").to(torch.bfloat16)
+        o = torch.empty_like(q)
+        q_start = torch.arange(0, S_ * L_ + 1, L_, dtype=torch.int32, device="cuda")
+        q_pos0 = torch.zeros(S_, dtype=torch.int32, device="cuda")
+        ws = torch.zeros(_lib.prefill_attention_workspace_bytes(), dtype=torch.uint8, device="cuda")
+        args_list = [_lib.prefill_attention_args(q, pool, table, q_start, q_pos0, o, H, KV, nb, BLOCK, L_, ws)]
+        call = _lib.paged_attention_prefill
+        flops = S_ * H * HEAD_DIM * 4.0 * L_ * (L_ + 1) / 2
     elif name == "gate_up_swiglu":
         act = torch.empty(B, I, device="cuda", dtype=torch.bfloat16)
         ws = torch.zeros(_lib.projection_workspace_bytes(B, D), dtype=torch.uint8, device="cuda")
@@ -1302,13 +1316,17 @@ def run_kernel(args, rank, world, local_rank):
     rc, bits = _lib.read_status(ws)
     if rc != 0:
         raise RuntimeError(f"{name} status {bits:#x}")
-    nbytes = stack_kernel_bytes(tp, ctx, B)[name][0]
     us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
     del graph, keep
     if rank == 0:
-        print(json.dumps({"workload": "kernel", "kernel": name, "tp_shapes": tp, "batch": B, "calls_per_graph": calls,
-                          "weight_copies": n, "us": round(us, 2), "algorithmic_bytes": nbytes,
-                          "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
+        line = {"workload": "kernel", "kernel": name, "tp_shapes": tp, "batch": B, "calls_per_graph": calls,
+                "weight_copies": n, "us": round(us, 2)}
+        if name == "prefill_attention":
+            line.update({"algorithmic_flops": int(flops), "TFLOPs": round(flops / us / 1e6, 1)})
+        else:
+            nbytes = stack_kernel_bytes(tp, ctx, B)[name][0]
+            line.update({"algorithmic_bytes": nbytes, "GBps": round(nbytes / us / 1e3, 1)})
+        print(json.dumps(line), flush=True)
 
 
 def run_reference_stack(args, world):
@@ -1339,7 +1357,7 @@ def main():
     ap.add_argument("--impl", choices=["krt", "reference"], default="krt")
     ap.add_argument("--kernel", default="paged_attention",
                     help="--workload kernel: paged_attention, qkv_rope_decode, o_proj_gemm_ar, gate_up_swiglu, "
-                         "down_proj_gemm_ar, lm_head_argmax")
+                         "down_proj_gemm_ar, lm_head_argmax, prefill_attention")
     ap.add_argument("--tp", type=int, default=0, help="--workload kernel: TP degree whose shard shapes to use")
     ap.add_argument("--batch", type=int, default=0, help="--workload kernel: tokens per call (default 128)")
     ap.add_argument("--model", choices=sorted(STACK_MODELS), default="8b",
