@@ -1225,8 +1225,9 @@ def run_kernel(args, rank, world, local_rank):
     from python.kinetic_rt.decoder import rope_cache
     torch.cuda.set_device(local_rank)
     tp = args.tp or world
-    B, ctx, D = args.batch or STACK_BATCH, PROMPT + GEN_STEPS // 2, HIDDEN
-    H, KV, I, V = N_HEADS // tp, N_KV // tp, INTER // tp, -(-VOCAB // tp)
+    _, D, H, KV, I, B0, P0, G0 = STACK_MODELS[args.model]
+    B, ctx = args.batch or B0, P0 + G0 // 2
+    H, KV, I, V = H // tp, KV // tp, I // tp, -(-VOCAB // tp)
     g = torch.Generator(device="cuda").manual_seed(0)
     x = torch.randn(B, D, generator=g, device="cuda").to(torch.bfloat16)
     gam = torch.ones(D, device="cuda", dtype=torch.bfloat16)
@@ -1319,12 +1320,13 @@ def run_kernel(args, rank, world, local_rank):
     us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
     del graph, keep
     if rank == 0:
-        line = {"workload": "kernel", "kernel": name, "tp_shapes": tp, "batch": B, "calls_per_graph": calls,
+        line = {"workload": "kernel", "kernel": name, "model": args.model, "tp_shapes": tp, "batch": B,
+                "calls_per_graph": calls,
                 "weight_copies": n, "us": round(us, 2)}
         if name == "prefill_attention":
             line.update({"algorithmic_flops": int(flops), "TFLOPs": round(flops / us / 1e6, 1)})
         else:
-            nbytes = stack_kernel_bytes(tp, ctx, B)[name][0]
+            nbytes = stack_kernel_bytes(tp, ctx, B, args.model)[name][0]
             line.update({"algorithmic_bytes": nbytes, "GBps": round(nbytes / us / 1e3, 1)})
         print(json.dumps(line), flush=True)
 

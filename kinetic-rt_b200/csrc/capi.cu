@@ -314,17 +314,24 @@ DecodeCfg decode_config(int heads, int num_kb, int n_pad, bool whole_tiles = fal
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  int tile_m = env_int("KRT_DECODE_TILE_M", heads <= 12 && n_pad <= 128 ? 64 : 128);
+  // Above 128 tokens whole-head tiles park 135 KB of partial and leave room
+  // for 2 splits only (B200, 256 tokens, 10 heads: 20 CTAs, 41.6 us); half
+  // heads need half of it: 24.7 us at 4 splits, 21.6 us at 6 (but 48 heads:
+  // 40.4 us against 29.0 on whole heads).
+  const bool wide = n_pad > 128;
+  int tile_m = env_int("KRT_DECODE_TILE_M", (heads <= 12 && !wide) || (heads <= 24 && wide) ? 64 : 128);
   if (tile_m != 64 || whole_tiles) tile_m = 128;
   const int tiles = heads * (128 / tile_m);
   DecodeCfg cfg{tile_m, tiles, 1, 1, 1};
   const int forced = env_int("KRT_DECODE_SPLITS", 0);
   // splits fill about two thirds of the SMs: more CTAs exchange more partials
   // than their extra streaming gains (B200, 64 tokens: 24 half-head tiles
-  // x 4 splits 10.1 us, x 6 splits 10.6 us)
+  // x 4 splits 10.1 us, x 6 splits 10.6 us); above 128 tokens five sixths
+  // (the 256-token case above)
   // (projections on whole tiles, gate/up at TP=8: 28 tiles x 4 splits 16.7 us,
   // x 3 splits 19.4 us, x 5 splits 26.4 us: about four fifths of the SMs)
-  int s = forced > 0 ? forced : device_sm_count() * (whole_tiles ? 4 : 2) / (whole_tiles ? 5 : 3) / tiles;
+  const int num = whole_tiles ? 4 : (wide ? 5 : 2), den = whole_tiles ? 5 : (wide ? 6 : 3);
+  int s = forced > 0 ? forced : device_sm_count() * num / den / tiles;
   if (s > 8) s = 8;
   if (s < 1) s = 1;
   for (; s >= 1; --s) {

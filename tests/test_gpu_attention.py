@@ -74,6 +74,15 @@ def test_attention_forced_splits(torch_cuda, monkeypatch):
     run_case(torch_cuda, [33, 64, 700, 5, 2048], 32, 8, seed=3)
 
 
+@pytest.mark.parametrize("lens,n_heads,n_kv_heads", [
+    ([8192], 4, 1),                     # one pair in many splits
+    ([1] * 300, 32, 8),                 # many one-token sequences
+    ([0] * 40 + [3000] * 2 + [17] * 30, 8, 1),  # long, short and empty sequences together
+], ids=["one_long", "many_short", "mixed"])
+def test_attention_shapes(torch_cuda, lens, n_heads, n_kv_heads):
+    run_case(torch_cuda, lens, n_heads, n_kv_heads, seed=len(lens))
+
+
 def test_attention_block_size_32_and_q_stride(torch_cuda):
     run_case(torch_cuda, [31, 32, 33, 500], 8, 2, seed=4, tokens_per_block=32, q_pad=64)
 

@@ -46,13 +46,15 @@ def _projection_kernel(monkeypatch, mode):
 
 @pytest.mark.parametrize("mode,T,I", [("splitk", 37, 320), ("tiles", 37, 320), ("streamk", 37, 320),
                                       ("auto", 128, 9600), ("tiles", 200, 704), ("streamk", 200, 704),
-                                      ("streamk", 64, 9600), ("auto", 700, 704), ("auto", 300, 9600)])
+                                      ("streamk", 64, 9600), ("auto", 700, 704), ("auto", 300, 9600),
+                                      ("tiles", 256, 9600)])
 def test_gate_up_swiglu(torch_cuda, monkeypatch, mode, T, I):
     """Split-K kernel (few tiles) and the persistent kernel: whole tiles (150
     tiles on 148 SMs gives two tiles to some CTAs, through both TMEM buffers)
     and stream-K (5 tiles of 4 k-boxes on 20 CTAs: every tile is one head
     and three partials; 150 tiles on 148 CTAs: runs of 4-5 boxes crossing
-    tile boundaries); prompts of 300 and 700 tokens run in 256-token blocks."""
+    tile boundaries); prompts of 300 and 700 tokens run in 256-token blocks;
+    256 tokens is one full block."""
     torch = torch_cuda
     from python.kinetic_rt import _lib
     _projection_kernel(monkeypatch, mode)

@@ -134,6 +134,21 @@ def test_paged_llama_shapes(torch_cuda, krt, kind, num_seqs, tokens_per_seq, ctx
         assert torch.equal(q1, d["q"])
 
 
+@pytest.mark.parametrize("num_seqs,d_model,n_heads,n_kv_heads", [
+    (256, 8192, 8, 1),   # Llama-3-70B TP=8 shard at decode batch 256 (half-head tiles above 128 tokens)
+    (200, 1024, 16, 2),  # 20 heads at 200 tokens
+    (144, 512, 32, 8),   # 48 heads above 128 tokens: whole-head tiles
+])
+def test_paged_decode_above_128_tokens(torch_cuda, krt, num_seqs, d_model, n_heads, n_kv_heads):
+    torch = torch_cuda
+    case = PagedCase(num_seqs, 1, d_model, n_heads, n_kv_heads, seed=num_seqs + n_heads, ctx=400)
+    d = case.to_device(torch)
+    _run_paged(krt, torch, case, d, "decode")
+    torch.cuda.synchronize()
+    check_outputs(case, d, torch)
+    check_pool(case, d, torch)
+
+
 @pytest.mark.parametrize("num_seqs,tokens_per_seq", [(1, 300), (3, 100)])
 def test_prefill_persistent_kernel(torch_cuda, krt, monkeypatch, num_seqs, tokens_per_seq):
     """KRT_PREFILL_KERNEL=1: the persistent projection kernel's QKV epilogue
