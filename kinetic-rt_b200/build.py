@@ -79,8 +79,10 @@ def build_lib(jobs=8):
         vs = os.path.join(objdir, "exports.map")
         with open(vs, "w") as f:
             f.write("{ global: krt_*; local: *; };\n")
+        tmp = out + ".tmp"  # linked aside and renamed: a reader never sees a half-written library
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-Xlinker", f"--version-script={vs}",
-              "-Xlinker", "--exclude-libs,ALL", *objs, "-o", out])
+              "-Xlinker", "--exclude-libs,ALL", *objs, "-o", tmp])
+        os.replace(tmp, out)
     return out
 
 
