@@ -345,47 +345,6 @@ DecodeCfg decode_config(int heads, int num_kb, int n_pad, bool whole_tiles = fal
   return cfg;
 }
 
-// The QKV decode with the split-K exchange through global memory instead of
-// a cluster (PagedParams::x2): the cluster tile of decode_config, as many
-// splits as give every SM one CTA (all splits of a tile are resident while
-// its owners wait for them), at most 16; taken when that is more than the
-// cluster split (48 heads at 128 tokens: 3 splits, 144 CTAs, where clusters
-// of 3 do not pack the GPCs and clusters of 2 leave 52 SMs idle).
-// KRT_DECODE_X2=1 / 0 turns it on / off.  splits = 0 when not taken.
-DecodeCfg decode_x2_config(int heads, int num_kb, int n_pad) {
-  const DecodeCfg c = decode_config(heads, num_kb, n_pad);
-  DecodeCfg x{c.tile_m, c.tiles, 1, 1, 0};
-  if (env_int("KRT_DECODE_X2", 0) == 0 || env_int("KRT_DECODE_SPLITS", 0) > 0) return x;
-  int s = device_sm_count() / c.tiles;
-  if (s > 16) s = 16;
-  for (; s > c.splits && s >= 2; --s) {
-    int kc = env_int("KRT_DECODE_KC", 4);
-    if (kc < 1) kc = 1;
-    int st = 0;
-    for (; kc >= 1; kc >>= 1) {
-      if (num_kb % kc != 0 || num_kb / kc < s) continue;
-      st = decode_stages(c.tile_m, n_pad, kc, 1);  // no receive area
-      if (st >= 2) break;
-    }
-    if (kc < 1 || st < 2) continue;
-    x.kc = kc;
-    x.stages = st;
-    x.splits = s;
-    return x;
-  }
-  return x;
-}
-
-// Workspace of the exchange: flags [tiles][splits][splits], then the slabs
-// [tiles][splits][n_pad][tile_m + 4] fp32.
-size_t x2_flags_bytes(const DecodeCfg& x) {
-  return ((size_t)x.tiles * x.splits * x.splits * 4 + 255) & ~size_t(255);
-}
-size_t x2_bytes(const DecodeCfg& x, int n_pad) {
-  if (x.splits == 0) return 0;
-  return x2_flags_bytes(x) + (size_t)x.tiles * x.splits * n_pad * (x.tile_m + 4) * 4;
-}
-
 }  // namespace
 
 namespace krt {
@@ -402,14 +361,10 @@ int decode_args_check(const krt_qkv_paged_args* a, const char* name) {
 
 extern "C" size_t krt_qkv_rope_decode_workspace_size(int32_t num_tokens, int32_t d_model, int32_t n_heads,
                                                      int32_t n_kv_heads, int32_t head_dim) {
-  if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0 || d_model % kBK != 0 || head_dim != kHeadDim ||
-      n_heads <= 0 || n_kv_heads <= 0)
+  if (num_tokens <= 0 || num_tokens > 256 || d_model <= 0 || head_dim != kHeadDim || n_heads <= 0 ||
+      n_kv_heads <= 0)
     return 0;
-  // the base layout, then room for the exchange through global memory (a
-  // workspace of the base size alone runs the cluster exchange)
-  const int n_pad = (num_tokens + 15) / 16 * 16;
-  const DecodeCfg x = decode_x2_config(n_heads + 2 * n_kv_heads, d_model / kBK, n_pad);
-  return ws_layout(num_tokens, d_model).total + x2_bytes(x, n_pad);
+  return ws_layout(num_tokens, d_model).total;
 }
 
 extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
@@ -419,9 +374,8 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
     return set_error(KRT_ERR_UNSUPPORTED, "krt_qkv_rope_decode: num_tokens must be <= 256 (use the prefill path)");
   const int tiles = a->n_heads + 2 * a->n_kv_heads;
   const int num_kb = a->d_model / kBK;
-  // the base layout is required; the exchange through global memory runs
-  // when the workspace also holds its flags and slabs
-  const size_t need = ws_layout(a->num_tokens, a->d_model).total;
+  const size_t need =
+      krt_qkv_rope_decode_workspace_size(a->num_tokens, a->d_model, a->n_heads, a->n_kv_heads, a->head_dim);
   if (a->workspace_bytes < need)
     return set_error(KRT_ERR_WORKSPACE, "krt_qkv_rope_decode: workspace of %zu bytes, %zu needed",
                      a->workspace_bytes, need);
@@ -452,15 +406,7 @@ extern "C" int krt_qkv_rope_decode(const krt_qkv_paged_args* a, void* stream) {
   p.num_blocks = a->num_blocks;
   p.tokens_per_block = a->tokens_per_block;
   p.eps = a->eps;
-  DecodeCfg cfg = decode_config(tiles, num_kb, p.n_pad);
-  const DecodeCfg x2 = decode_x2_config(tiles, num_kb, p.n_pad);
-  if (x2.splits > 0 && a->workspace_bytes >= need + x2_bytes(x2, p.n_pad)) {
-    cfg = x2;
-    p.x2 = 1;
-    char* xw = static_cast<char*>(a->workspace) + need;
-    p.x2_flags = reinterpret_cast<uint32_t*>(xw);
-    p.x2_part = reinterpret_cast<float*>(xw + x2_flags_bytes(x2));
-  }
+  const DecodeCfg cfg = decode_config(tiles, num_kb, p.n_pad);
   p.kc = cfg.kc;
   p.stages = cfg.stages;
   p.splits = cfg.splits;

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   uint8_t* b_smem = smem + (size_t)S * a_stage;
   uint8_t* recv_smem = smem + decode_pipe_bytes<TM>(S, n_pad, KC);
   DecodeSmemTail* tl =
-      reinterpret_cast<DecodeSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.x2 ? 1 : p.splits, TS::kChunkBytes));
+      reinterpret_cast<DecodeSmemTail*>(recv_smem + recv_area_bytes(n_pad, p.splits, TS::kChunkBytes));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -157,9 +157,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     }
     for (int i = pre; i < nk && i < pre + p.prefetch; ++i) prefetch_w(i);
     // the partials this CTA will receive: (splits - 1) per owned chunk
-    if (!p.x2)
-      mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
-                                           TS::kChunkBytes);
+    mbar_arrive_expect_tx(&tl->recv, (uint32_t)(owned_chunks(n_pad / 16, p.splits, split) * (p.splits - 1)) *
+                                         TS::kChunkBytes);
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
@@ -169,7 +168,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (!p.x2) cluster_arrive_relaxed();  // the receive barriers are initialised; waited on before the first push
+  cluster_arrive_relaxed();  // the receive barriers are initialised; waited on before the first push
   // The next kernel may launch onto free SMs now; it waits for this grid
   // (griddepcontrol.wait) before touching anything this kernel writes.
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -275,10 +274,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     const bool waited = mbar_wait_warp(&tl->accum, 0u, abort_flag);
     if (!waited && lane == 0) decode_fail(p, tl, kStatusTimeoutAccum);
     tc_fence_after();
-    if (!p.x2) cluster_wait();
-    // exchange through global memory: this split's slab and its tile's flags
-    float* x2_slabs = p.x2 ? p.x2_part + (size_t)tile * nranks * n_pad * YS : nullptr;
-    uint32_t* x2_fl = p.x2 ? p.x2_flags + (size_t)tile * nranks * nranks : nullptr;
+    cluster_wait();
 
     // Park the partial token-major in the idle pipeline buffers, four 16-token
     // chunks at a time; a chunk finished by another rank is sent to it by
@@ -298,23 +294,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc)
             if (cc < nc) {
-              const int c = c0 + cc;
-              if (p.x2 && c % nranks != rank) {
-                // another split finishes this chunk: straight to this split's slab
-                // (a warp stores 32 consecutive rows of a token: 128 B)
-                float* dst = x2_slabs + (size_t)rank * n_pad * YS + (size_t)(c * 16) * YS + r;
 #pragma unroll
-                for (int jj = 0; jj < 16; ++jj) __stcg(dst + (size_t)jj * YS, __uint_as_float(v[cc][jj]));
-              } else {
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj) part[(c * 16 + jj) * YS + r] = __uint_as_float(v[cc][jj]);
-              }
+              for (int jj = 0; jj < 16; ++jj) part[((c0 + cc) * 16 + jj) * YS + r] = __uint_as_float(v[cc][jj]);
             }
         }
       }
       bool remote = false;
       for (int cc = 0; cc < nc; ++cc) remote |= (c0 + cc) % nranks != rank;
-      if (remote && !p.x2) {
+      if (remote) {
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         // chunk cc of the group is sent by lane 0 of epilogue warp cc, so the
@@ -333,26 +320,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       }
     }
     if ((ept & 31) == 0) bulk_commit_group();
-    named_bar_sync(1, 128);  // the owned chunks are parked (and the slab written)
-    if (p.x2 && ept == 0) {
-      // raised also after a failed accumulator wait, so that no owner waits out its budget
-      __threadfence();
-      for (int q = 0; q < nranks; ++q)
-        if (q != rank) st_release_gpu(x2_fl + (size_t)rank * nranks + q, 1u);
-    }
+    named_bar_sync(1, 128);  // the owned chunks are parked
 
     // ------------------------------------------------ finish the owned chunks
-    bool got;
-    if (p.x2) {
-      // every split of the tile is resident (grid <= #SMs, one CTA per SM)
-      bool ok = true;
-      if (ept == 0)
-        for (int q = 0; q < nranks && ok; ++q)
-          if (q != rank) ok = wait_flag_gpu(x2_fl + (size_t)q * nranks + rank, 1u);
-      got = !named_bar_any(1, 128, !ok);
-    } else {
-      got = mbar_wait_warp_incoming(&tl->recv, 0u);
-    }
+    const bool got = mbar_wait_warp_incoming(&tl->recv, 0u);
     if (!got && lane == 0) decode_fail(p, tl, kStatusTimeoutCluster);
     if (got && *abort_flag == 0) {
       const float* recv = reinterpret_cast<const float*>(recv_smem);
@@ -387,17 +358,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             const int q = q0 + qq < nranks ? q0 + qq : q0;
-            if (p.x2 && q != rank) {
-              const float* src = x2_slabs + ((size_t)q * n_pad + t) * YS;  // written by another CTA: via L2
-#pragma unroll
-              for (int k4 = 0; k4 < RG / 4; ++k4) a[qq][k4] = __ldcg(reinterpret_cast<const float4*>(src + RG * g) + k4);
-              if (rot) {
-#pragma unroll
-                for (int k4 = 0; k4 < RG / 4; ++k4)
-                  b[qq][k4] = __ldcg(reinterpret_cast<const float4*>(src + RG * gp) + k4);
-              }
-              continue;
-            }
             const float* src = q == rank ? part + t * YS
                                          : recv + (size_t)recv_slot(oc, nranks, rank, q) * (TS::kChunkBytes / 4) +
                                                (size_t)j * YS;
@@ -449,14 +409,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       for (int t = ept; t < T; t += 128)
         if (tl->key[t] != 0ull) atomicMax(p.keys + t, tl->key[t]);
     }
-    // the consumed flags go back to 0 for the next launch
-    if (p.x2 && got && ept == 0)
-      for (int q = 0; q < nranks; ++q)
-        if (q != rank) x2_fl[(size_t)q * nranks + rank] = 0u;
     if ((ept & 31) == 0) bulk_wait_group_read0();  // the sent chunks have left this CTA's shared memory
   }
 
-  if (warp < 2 && !p.x2) cluster_wait();
+  if (warp < 2) cluster_wait();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -479,7 +435,7 @@ size_t decode_smem_bytes(int tile_m, int stages, int n_pad, int kc, int splits) 
 template <int TM, int EPI>
 static cudaError_t launch_decode_t(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const PagedParams& p,
                                    int tiles, cudaStream_t stream) {
-  const size_t smem = decode_smem_bytes_t<TM>(p.stages, p.n_pad, p.kc, p.x2 ? 1 : p.splits);
+  const size_t smem = decode_smem_bytes_t<TM>(p.stages, p.n_pad, p.kc, p.splits);
   cudaError_t e =
       cudaFuncSetAttribute(qkv_rope_decode_kernel<TM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -496,7 +452,7 @@ static cudaError_t launch_decode_t(const CUtensorMap& tmap_w, const CUtensorMap&
   attr[1].val.clusterDim.y = (unsigned)p.splits;
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = p.x2 ? 1 : 2;  // the global-memory exchange runs without a cluster
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, qkv_rope_decode_kernel<TM, EPI>, tmap_w, tmap_x, p);
 }
 

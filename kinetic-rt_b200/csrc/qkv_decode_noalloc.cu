@@ -98,9 +98,8 @@ extern "C" int krt_qkv_rope_decode_noalloc(const krt_qkv_paged_args* args, void*
   // GPU nor the shared array.
   int rc = decode_args_check(args, name);
   if (rc) return rc;
-  // the base layout (status, metadata, normalised activations); the split-K
-  // exchange through global memory only runs when the scratch also holds it
-  const size_t need = ws_layout(args->num_tokens, args->d_model).total;
+  const size_t need = krt_qkv_rope_decode_workspace_size(args->num_tokens, args->d_model, args->n_heads,
+                                                         args->n_kv_heads, args->head_dim);
   if (need == 0 || need > kNoAllocScratchBytes)
     return set_error(KRT_ERR_UNSUPPORTED,
                      "%s: this call needs %zu bytes of scratch (num_tokens %d, d_model %d); "

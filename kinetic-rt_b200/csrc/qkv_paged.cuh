@@ -61,14 +61,6 @@ struct PagedParams {
   // Persistent projection kernel over token blocks of n_pad tokens:
   // tile = block * row_tiles + row tile (row_tiles 0: one token block).
   int row_tiles;
-  // Split-K decode kernel, exchange through global memory (x2 != 0) instead
-  // of a thread-block cluster: split q of a tile writes the 16-token chunks
-  // that other splits finish to x2_part[tile][q] ([n_pad][TM + 4] fp32,
-  // token-major) and raises x2_flags[tile][q][owner]; the owner clears it
-  // once consumed.
-  int x2;
-  float* x2_part;
-  uint32_t* x2_flags;
   __nv_bfloat16* y;     // kEpiStore: [num_tokens, y_stride] bf16(acc + residual)
   int y_stride;
   const __nv_bfloat16* residual;  // kEpiStore: optional, same layout as y

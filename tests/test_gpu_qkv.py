@@ -134,30 +134,6 @@ def test_paged_llama_shapes(torch_cuda, krt, kind, num_seqs, tokens_per_seq, ctx
         assert torch.equal(q1, d["q"])
 
 
-@pytest.mark.parametrize("x2", ["1", "0"], ids=["global_exchange", "cluster_exchange"])
-@pytest.mark.parametrize("num_seqs,n_heads,n_kv_heads", [
-    (128, 32, 8),   # 48 whole-head tiles: 3 splits through global memory, 2 in clusters
-    (64, 4, 1),     # TP=8 shard: 12 half-head tiles, 12 splits through global memory
-    (200, 16, 2),   # 20 whole-head tiles at 200 tokens
-    (7, 32, 8),     # one 16-token chunk: only split 0 owns a chunk
-])
-def test_paged_decode_exchange_modes(torch_cuda, krt, monkeypatch, x2, num_seqs, n_heads, n_kv_heads):
-    """The split-K partials exchanged through global memory (flags per
-    (tile, split, owner), no cluster) and through cluster shared memory give
-    the oracle's outputs; three calls on one workspace with new inputs each
-    time (the flags go back to 0 after every call)."""
-    torch = torch_cuda
-    monkeypatch.setenv("KRT_DECODE_X2", x2)
-    ws = None
-    for step in range(3):
-        case = PagedCase(num_seqs, 1, 1024, n_heads, n_kv_heads, seed=100 * step + num_seqs, ctx=300 + step)
-        d = case.to_device(torch)
-        ws = _run_paged(krt, torch, case, d, "decode", workspace=ws)
-        torch.cuda.synchronize()
-        check_outputs(case, d, torch)
-        check_pool(case, d, torch)
-
-
 @pytest.mark.parametrize("num_seqs,d_model,n_heads,n_kv_heads", [
     (256, 8192, 8, 1),   # Llama-3-70B TP=8 shard at decode batch 256 (half-head tiles above 128 tokens)
     (200, 1024, 16, 2),  # 20 heads at 200 tokens
